@@ -1,0 +1,159 @@
+/*
+ * vmps.h -- C ABI of libvmps_kernels.so, the sm_100a (B200) kernels behind
+ * the paged decode-attention step of vllm_mps.
+ *
+ * The reference (Nihar0071/vllm_mps) has no C ABI: its device code is two
+ * Metal shaders held as Python strings and its CPU path is PyTorch code.
+ * Each entry point below names the reference interface it replaces.  The
+ * Python side binds these symbols with ctypes (vllm_mps_b200/kernels).
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers unless stated; the caller owns every
+ *     buffer (the library allocates nothing and keeps no per-call state
+ *     except the device error word).
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Work is
+ *     only enqueued; calls return before the GPU finishes.
+ *   - `dtype` is VMPS_DTYPE_F16 or VMPS_DTYPE_BF16 for every 16-bit tensor
+ *     of the call (q, k, v, pool, out).
+ *   - The KV pool has the reference layout
+ *       pool[num_blocks][2][block_size][n_kv][head_dim]   (dim 1: 0 = K, 1 = V)
+ *     (memory/mps_memory_pool.py:62-66), contiguous.
+ *   - Return 0 on success or a negative VMPS_ERR_* code; vmps_last_error()
+ *     then describes the failure (thread-local).  Arguments are checked on
+ *     the host before anything is launched.  Device-side index violations
+ *     skip the access and set a bit in the error word (vmps_debug_error_word).
+ */
+#ifndef VMPS_H_
+#define VMPS_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VMPS_OK 0
+#define VMPS_ERR_INVALID_ARG (-1)  /* bad pointer, size or shape */
+#define VMPS_ERR_UNSUPPORTED (-2)  /* valid but not built (e.g. head_dim 96) */
+#define VMPS_ERR_ALIGNMENT (-3)    /* a pointer or stride is not 16-byte aligned */
+#define VMPS_ERR_WORKSPACE (-4)    /* workspace missing or too small */
+#define VMPS_ERR_CUDA (-5)         /* CUDA runtime/driver error */
+
+#define VMPS_DTYPE_F16 0
+#define VMPS_DTYPE_BF16 1
+
+/* Library version string, e.g. "vmps 0.1.0 sm_100a". */
+const char* vmps_version(void);
+
+/* Description of the last failure on the calling thread ("" if none). */
+const char* vmps_last_error(void);
+
+/*
+ * Fused RoPE + reshape-and-cache (kernel 1).
+ *
+ * Replaces the per-sequence RoPE loop and K/V write loop of
+ * PagedAttentionLayer._forward_batch (layers/paged_attention_layer.py:275-286
+ * and :317-324), i.e. RotaryEmbedding.forward (layers/rotary_embedding.py:55-76)
+ * followed by MPSMemoryPool.write_kv (memory/mps_memory_pool.py:82-102), and
+ * Phase 1 of the Metal fused_attention shader (kernels/__init__.py:139-161).
+ *
+ * For each sequence i in [0, num_seqs):
+ *   q_out[i] = rope(q[i], positions[i])                  (n_q heads)
+ *   pool[slot / block_size][0][slot % block_size] = rope(k[i], positions[i])
+ *   pool[slot / block_size][1][slot % block_size] = v[i]
+ * with slot = slot_mapping[i] (= block_table[pos / block_size] * block_size
+ * + pos % block_size); a negative slot skips the write.  rope() is the
+ * rotate-half form with cos/sin = cos/sin(position * inv_freq[j]) rounded
+ * to the model dtype and each product and the sum rounded to the model
+ * dtype, as the reference computes it.  inv_freq (head_dim/2 floats) = NULL
+ * means "no rotation" (K/V are written as given, q_out = q).
+ *
+ * q/k/v rows are head-major [heads][head_dim] with a row stride in elements
+ * between sequences (so slices of a fused QKV output work).  q_out may equal
+ * q (in-place) and uses q_row_stride too.  positions and slot_mapping are
+ * int32[num_seqs] on the device.
+ */
+int vmps_rope_reshape_and_cache(void* q_out, const void* q, int64_t q_row_stride,
+                                const void* k, int64_t k_row_stride, const void* v,
+                                int64_t v_row_stride, const int32_t* positions,
+                                const int32_t* slot_mapping, const float* inv_freq, void* pool,
+                                int num_seqs, int n_q, int n_kv, int head_dim, int block_size,
+                                int num_blocks, int dtype, void* stream);
+
+/*
+ * Workspace needed by vmps_paged_decode_attention on the current device for
+ * up to `num_seqs` sequences (the split-K partial results of sequences cut
+ * between CTAs, and the work split the combine step reads).  Its contents
+ * need no initialisation; calls sharing a workspace must be ordered (same
+ * stream).  Returns 0 if the shape is unsupported.
+ */
+size_t vmps_paged_decode_workspace_bytes(int num_seqs, int n_q, int n_kv, int head_dim,
+                                         int dtype);
+
+/* cudaMemsetAsync(workspace, 0, bytes, stream); optional (kept for callers
+ * that want a deterministic initial state). */
+int vmps_paged_decode_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Paged decode attention (kernel 2), one query token per sequence.
+ *
+ * Replaces the gather/pad loop, GQA expansion and masked softmax attention of
+ * PagedAttentionLayer._forward_batch (layers/paged_attention_layer.py:326-359),
+ * MPSMemoryPool.gather_blocks_tensor (memory/mps_memory_pool.py:159-176), and
+ * Phases 2-4 of the Metal fused_attention shader (kernels/__init__.py:166-241).
+ *
+ *   out[i][h][:] = softmax_t( scale * q[i][h] . K_i[t][h / G] ) . V_i[t][h / G]
+ * for t < seq_lens[i], G = n_q / n_kv, where K_i[t] / V_i[t] is slot
+ * t % block_size of block block_tables[i * max_blocks_per_seq + t / block_size].
+ * Computed with fp32 scores, fp32 online softmax and fp32 accumulation;
+ * out is rounded once to the model dtype.  q and out are [num_seqs][n_q][head_dim]
+ * contiguous; seq_lens counts the new token; block tables are int32, only
+ * the first ceil(seq_len / block_size) entries of a row are read.  A
+ * sequence with seq_len 0 gets a zero output row.
+ *
+ * Supported: head_dim 64 or 128, block_size 16, n_q / n_kv in {1,2,4,8,16},
+ * num_seqs <= 4096.  Long sequences are split across CTAs (flash-decoding);
+ * a second, small kernel merges the pieces.  Both are launched with
+ * programmatic dependent launch (they wait for the preceding kernel's writes
+ * before reading q or the pool).
+ */
+int vmps_paged_decode_attention(void* out, const void* q, const void* pool,
+                                const int32_t* block_tables, int max_blocks_per_seq,
+                                const int32_t* seq_lens, int num_seqs, int n_q, int n_kv,
+                                int head_dim, int block_size, int num_blocks, float scale,
+                                void* workspace, size_t workspace_bytes, int dtype, void* stream);
+
+/*
+ * One decode step of one attention layer: kernel 1 then kernel 2 on `stream`.
+ *
+ * Equivalent to vmps_rope_reshape_and_cache(q, q, ...) (Q rotated in place,
+ * rotated K and V written to the pool) followed by
+ * vmps_paged_decode_attention(out, q, ...), i.e. PagedAttentionLayer's
+ * batched step between its projections (layers/paged_attention_layer.py:275-359)
+ * and the whole Metal fused_attention shader (kernels/__init__.py:99-242)
+ * with RoPE folded in.  Because the attention kernel knows its predecessor
+ * only writes q and the pool, it reads seq_lens while kernel 1 is still
+ * running.  q must be packed (q_row_stride == n_q * head_dim).
+ */
+int vmps_paged_decode_step(void* out, void* q, int64_t q_row_stride, const void* k,
+                           int64_t k_row_stride, const void* v, int64_t v_row_stride,
+                           const int32_t* positions, const int32_t* slot_mapping,
+                           const float* inv_freq, void* pool, const int32_t* block_tables,
+                           int max_blocks_per_seq, const int32_t* seq_lens, int num_seqs, int n_q,
+                           int n_kv, int head_dim, int block_size, int num_blocks, float scale,
+                           void* workspace, size_t workspace_bytes, int dtype, void* stream);
+
+/*
+ * Reads and clears the device error word of the current device (a bitwise OR
+ * of index violations the kernels skipped since the last call).  Synchronises
+ * `stream`.  Bits: 1 slot out of range, 2 block id out of range, 4 seq_len
+ * beyond the block table, 8 an internal wait timed out, 16 negative position.
+ */
+int vmps_debug_error_word(void* stream, int* word_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VMPS_H_ */

@@ -1,0 +1,40 @@
+"""Shared test configuration: the ``gpu`` marker and fixture helpers."""
+
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+def load_golden(name: str):
+    return np.load(os.path.join(GOLDEN, name), allow_pickle=False)
+
+
+def golden_pool_bits(d) -> np.ndarray:
+    """Regenerate the seeded pool of an ``attn_*.npz`` fixture (uint16 bits)."""
+    from oracle.paged_attention_oracle import f32_to_bits
+
+    shape = (int(d["num_blocks"]), 2, int(d["block_size"]), int(d["n_kv"]), int(d["D"]))
+    rng = np.random.default_rng(int(d["pool_seed"]))
+    x = rng.standard_normal(size=shape, dtype=np.float32)
+    return f32_to_bits(x, str(d["dtype"]))
+
+
+@pytest.fixture(scope="session")
+def cuda_device():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.fail("this test needs a CUDA device")
+    return torch.device("cuda", 0)

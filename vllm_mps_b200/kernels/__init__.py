@@ -1,0 +1,404 @@
+"""Python bindings of libvmps_kernels.so (the sm_100a kernels of the decode step).
+
+This module replaces the reference's ``vllm_mps.kernels`` (Metal shaders
+compiled through ``torch.mps.compile_shader``, kernels/__init__.py:245-406).
+It binds the C ABI declared in ``include/vmps.h`` with ctypes and passes raw
+device pointers plus the current CUDA stream.  There is no CPU or PyTorch
+fallback: if the shared library is missing or a tensor is not on a CUDA
+device, the call raises.
+
+Public functions
+----------------
+* :func:`rope_reshape_and_cache` -- kernel 1 (RoPE on Q/K + K/V write).
+* :func:`paged_decode_attention` -- kernel 2 (paged GQA decode attention).
+* :func:`fused_attention` / :func:`fused_attention_metal_fast` -- the
+  reference's fused entry point (kernels/__init__.py:320-368): write the
+  already-rotated new K/V into the slot given by ``write_info`` and attend.
+* :func:`gather_kv` -- the reference's padded paged gather
+  (kernels/__init__.py:279-312), kept for API compatibility.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import threading
+
+import torch
+
+_PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(_PKG_DIR, "libvmps_kernels.so")
+
+VMPS_DTYPE_F16 = 0
+VMPS_DTYPE_BF16 = 1
+
+_ERRORS = {
+    -1: ValueError,        # VMPS_ERR_INVALID_ARG
+    -2: NotImplementedError,  # VMPS_ERR_UNSUPPORTED
+    -3: ValueError,        # VMPS_ERR_ALIGNMENT
+    -4: RuntimeError,      # VMPS_ERR_WORKSPACE
+    -5: RuntimeError,      # VMPS_ERR_CUDA
+}
+
+#: Symbols every build of the library exports (mirrors include/vmps.h).
+EXPORTED_SYMBOLS = (
+    "vmps_version",
+    "vmps_last_error",
+    "vmps_rope_reshape_and_cache",
+    "vmps_paged_decode_workspace_bytes",
+    "vmps_paged_decode_workspace_init",
+    "vmps_paged_decode_attention",
+    "vmps_paged_decode_step",
+    "vmps_debug_error_word",
+)
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def load_library(path: str | None = None) -> ctypes.CDLL:
+    """Load (once) and return the kernel library, declaring every signature."""
+    global _lib
+    with _lib_lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise ImportError(
+                f"{p} is missing: build it with `python -m vllm_mps_b200.build` "
+                "(there is no CPU fallback for the CUDA kernels)")
+        lib = ctypes.CDLL(p)
+        vp, i32, i64, f32, sz = (ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
+                                 ctypes.c_float, ctypes.c_size_t)
+        lib.vmps_version.restype = ctypes.c_char_p
+        lib.vmps_version.argtypes = []
+        lib.vmps_last_error.restype = ctypes.c_char_p
+        lib.vmps_last_error.argtypes = []
+        lib.vmps_rope_reshape_and_cache.restype = i32
+        lib.vmps_rope_reshape_and_cache.argtypes = [
+            vp, vp, i64, vp, i64, vp, i64, vp, vp, vp, vp,
+            i32, i32, i32, i32, i32, i32, i32, vp]
+        lib.vmps_paged_decode_workspace_bytes.restype = sz
+        lib.vmps_paged_decode_workspace_bytes.argtypes = [i32, i32, i32, i32, i32]
+        lib.vmps_paged_decode_workspace_init.restype = i32
+        lib.vmps_paged_decode_workspace_init.argtypes = [vp, sz, vp]
+        lib.vmps_paged_decode_attention.restype = i32
+        lib.vmps_paged_decode_attention.argtypes = [
+            vp, vp, vp, vp, i32, vp, i32, i32, i32, i32, i32, i32, f32, vp, sz, i32, vp]
+        lib.vmps_paged_decode_step.restype = i32
+        lib.vmps_paged_decode_step.argtypes = [
+            vp, vp, i64, vp, i64, vp, i64, vp, vp, vp, vp, vp, i32, vp,
+            i32, i32, i32, i32, i32, i32, f32, vp, sz, i32, vp]
+        lib.vmps_debug_error_word.restype = i32
+        lib.vmps_debug_error_word.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load_library().vmps_last_error().decode(errors="replace")
+        raise _ERRORS.get(rc, RuntimeError)(f"{what}: {msg or 'error %d' % rc}")
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    if dtype == torch.float16:
+        return VMPS_DTYPE_F16
+    if dtype == torch.bfloat16:
+        return VMPS_DTYPE_BF16
+    raise TypeError(f"unsupported dtype {dtype} (float16 or bfloat16)")
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(
+                f"vllm_mps_b200 kernels need CUDA tensors (got a {t.device} tensor); "
+                "there is no CPU fallback")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _int32(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype != torch.int32:
+        raise TypeError(f"{name} must be int32 (got {t.dtype})")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+def _check_pool(pool: torch.Tensor):
+    if pool.dim() != 5 or pool.shape[1] != 2:
+        raise ValueError(f"pool must be (num_blocks, 2, block_size, n_kv, head_dim); got {tuple(pool.shape)}")
+    if not pool.is_contiguous():
+        raise ValueError("pool must be contiguous")
+    return pool.shape[0], pool.shape[2], pool.shape[3], pool.shape[4]
+
+
+def _rows(t: torch.Tensor, heads: int, d: int, name: str):
+    """(B, heads, d) or (B, heads*d) view with unit inner strides -> row stride."""
+    if t.dim() == 3:
+        if t.shape[1:] != (heads, d) or t.stride(2) != 1 or t.stride(1) != d:
+            raise ValueError(f"{name}: expected (B, {heads}, {d}) with packed heads")
+        return t.stride(0)
+    if t.dim() == 2:
+        if t.shape[1] != heads * d or t.stride(1) != 1:
+            raise ValueError(f"{name}: expected (B, {heads * d})")
+        return t.stride(0)
+    raise ValueError(f"{name}: expected 2-D or 3-D tensor")
+
+
+# ── kernel 1 ─────────────────────────────────────────────────────────────────
+
+
+def rope_reshape_and_cache(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                           positions: torch.Tensor | None, slot_mapping: torch.Tensor,
+                           inv_freq: torch.Tensor | None, pool: torch.Tensor,
+                           q_out: torch.Tensor | None = None) -> torch.Tensor:
+    """RoPE on q and k, then write rotated k and v into ``pool`` at ``slot_mapping``.
+
+    ``q``: (B, n_q, D) or (B, n_q*D); ``k``/``v``: (B, n_kv, D) or (B, n_kv*D)
+    (row strides may be larger, e.g. slices of a fused QKV output).
+    ``positions``/``slot_mapping``: int32 (B,).  ``inv_freq``: fp32 (D/2,) or
+    None (no rotation).  Returns ``q_out`` (default: ``q`` rotated in place).
+    Same semantics as the reference's per-sequence loop
+    (layers/paged_attention_layer.py:275-286, :317-324).
+    """
+    num_blocks, block_size, n_kv, D = _check_pool(pool)
+    B = k.shape[0]
+    n_q = (q.shape[1] if q.dim() == 3 else q.shape[1] // D) if q is not None else 0
+    if q_out is None:
+        q_out = q
+    dev = _require_cuda(q, k, v, positions, slot_mapping, inv_freq, pool, q_out)
+    for t, name in ((q, "q"), (k, "k"), (v, "v"), (q_out, "q_out")):
+        if t is not None and t.dtype != pool.dtype:
+            raise TypeError(f"{name} dtype {t.dtype} != pool dtype {pool.dtype}")
+    qs = _rows(q, n_q, D, "q") if n_q else 0
+    if q_out is not q and n_q:
+        if _rows(q_out, n_q, D, "q_out") != qs:
+            raise ValueError("q_out must have the same row stride as q")
+    ks = _rows(k, n_kv, D, "k")
+    vs = _rows(v, n_kv, D, "v")
+    _int32(slot_mapping, "slot_mapping")
+    if positions is not None:
+        _int32(positions, "positions")
+    if inv_freq is not None:
+        if inv_freq.dtype != torch.float32 or inv_freq.numel() != D // 2 or not inv_freq.is_contiguous():
+            raise ValueError(f"inv_freq must be contiguous float32 of {D // 2} entries")
+    lib = load_library()
+    with torch.cuda.device(dev):
+        rc = lib.vmps_rope_reshape_and_cache(
+            _ptr(q_out), _ptr(q), qs, _ptr(k), ks, _ptr(v), vs, _ptr(positions),
+            _ptr(slot_mapping), _ptr(inv_freq), _ptr(pool), B, n_q, n_kv, D, block_size,
+            num_blocks, dtype_code(pool.dtype), _stream(dev))
+    _check(rc, "rope_reshape_and_cache")
+    return q_out
+
+
+# ── kernel 2 ─────────────────────────────────────────────────────────────────
+
+
+class DecodeWorkspace:
+    """Scratch buffer for :func:`paged_decode_attention`, grown on demand.
+
+    Holds the split-K partial results of one call; one buffer is reused
+    across calls on the same stream.  Calls on different streams that may
+    overlap need different workspaces.
+    """
+
+    def __init__(self) -> None:
+        self._buf: dict[torch.device, torch.Tensor] = {}
+
+    def get(self, device: torch.device, num_seqs: int, n_q: int, n_kv: int, d: int,
+            dtype: torch.dtype) -> torch.Tensor:
+        lib = load_library()
+        with torch.cuda.device(device):
+            need = lib.vmps_paged_decode_workspace_bytes(num_seqs, n_q, n_kv, d, dtype_code(dtype))
+        if need == 0:
+            raise NotImplementedError(
+                f"paged_decode_attention: n_q={n_q} n_kv={n_kv} head_dim={d} not supported")
+        buf = self._buf.get(device)
+        if buf is None or buf.numel() < need:
+            # Grow geometrically; torch allocations are 512-byte aligned.
+            size = max(need, 0 if buf is None else 2 * buf.numel())
+            buf = torch.empty(size, dtype=torch.uint8, device=device)
+            self._buf[device] = buf
+        return buf
+
+
+_default_workspace = DecodeWorkspace()
+
+
+def paged_decode_attention(q: torch.Tensor, pool: torch.Tensor, block_tables: torch.Tensor,
+                           seq_lens: torch.Tensor, scale: float | None = None,
+                           out: torch.Tensor | None = None,
+                           workspace: DecodeWorkspace | torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention of one query token per sequence over its paged K/V.
+
+    ``q``: (B, n_q, D) contiguous; ``pool``: (num_blocks, 2, 16, n_kv, D);
+    ``block_tables``: int32 (B, max_blocks) zero-padded; ``seq_lens``: int32
+    (B,) counting the new token.  Returns ``out`` (B, n_q, D) in the pool
+    dtype.  ``scale`` defaults to ``1/sqrt(D)`` (layers/paged_attention_layer.py:353).
+    """
+    num_blocks, block_size, n_kv, D = _check_pool(pool)
+    if q.dim() != 3 or q.shape[2] != D or not q.is_contiguous():
+        raise ValueError(f"q must be contiguous (B, n_q, {D}); got {tuple(q.shape)}")
+    B, n_q = q.shape[0], q.shape[1]
+    if block_tables.dim() != 2 or block_tables.shape[0] != B:
+        raise ValueError("block_tables must be (B, max_blocks)")
+    if seq_lens.numel() != B:
+        raise ValueError("seq_lens must have B entries")
+    if q.dtype != pool.dtype:
+        raise TypeError(f"q dtype {q.dtype} != pool dtype {pool.dtype}")
+    _int32(block_tables, "block_tables")
+    _int32(seq_lens, "seq_lens")
+    if out is None:
+        out = torch.empty_like(q)
+    elif out.shape != q.shape or out.dtype != q.dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous tensor like q")
+    dev = _require_cuda(q, pool, block_tables, seq_lens, out)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if isinstance(workspace, torch.Tensor):
+        ws = workspace
+    else:
+        ws = (workspace or _default_workspace).get(dev, B, n_q, n_kv, D, pool.dtype)
+    lib = load_library()
+    with torch.cuda.device(dev):
+        rc = lib.vmps_paged_decode_attention(
+            _ptr(out), _ptr(q), _ptr(pool), _ptr(block_tables), block_tables.shape[1],
+            _ptr(seq_lens), B, n_q, n_kv, D, block_size, num_blocks, float(scale),
+            _ptr(ws), ws.numel() * ws.element_size(), dtype_code(pool.dtype), _stream(dev))
+    _check(rc, "paged_decode_attention")
+    return out
+
+
+def paged_decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      positions: torch.Tensor, slot_mapping: torch.Tensor,
+                      inv_freq: torch.Tensor | None, pool: torch.Tensor,
+                      block_tables: torch.Tensor, seq_lens: torch.Tensor,
+                      scale: float | None = None, out: torch.Tensor | None = None,
+                      workspace: DecodeWorkspace | torch.Tensor | None = None) -> torch.Tensor:
+    """One decode step of one layer: RoPE + cache write, then paged attention.
+
+    ``q`` (B, n_q, D) contiguous is rotated in place; ``k``/``v`` (B, n_kv, D)
+    (any row stride) are written to ``pool`` at ``slot_mapping``.  Returns the
+    attention output (B, n_q, D).  Replaces PagedAttentionLayer._forward_batch
+    between its projections (layers/paged_attention_layer.py:275-359).
+    """
+    num_blocks, block_size, n_kv, D = _check_pool(pool)
+    if q.dim() != 3 or q.shape[2] != D or not q.is_contiguous():
+        raise ValueError(f"q must be contiguous (B, n_q, {D})")
+    B, n_q = q.shape[0], q.shape[1]
+    ks = _rows(k, n_kv, D, "k")
+    vs = _rows(v, n_kv, D, "v")
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        if t.dtype != pool.dtype:
+            raise TypeError(f"{name} dtype {t.dtype} != pool dtype {pool.dtype}")
+    _int32(positions, "positions")
+    _int32(slot_mapping, "slot_mapping")
+    _int32(block_tables, "block_tables")
+    _int32(seq_lens, "seq_lens")
+    if block_tables.dim() != 2 or block_tables.shape[0] != B or seq_lens.numel() != B:
+        raise ValueError("block_tables must be (B, max_blocks) and seq_lens (B,)")
+    if inv_freq is not None and (inv_freq.dtype != torch.float32 or inv_freq.numel() != D // 2):
+        raise ValueError(f"inv_freq must be float32 of {D // 2} entries")
+    if out is None:
+        out = torch.empty_like(q)
+    dev = _require_cuda(q, k, v, positions, slot_mapping, inv_freq, pool, block_tables,
+                        seq_lens, out)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if isinstance(workspace, torch.Tensor):
+        ws = workspace
+    else:
+        ws = (workspace or _default_workspace).get(dev, B, n_q, n_kv, D, pool.dtype)
+    lib = load_library()
+    with torch.cuda.device(dev):
+        rc = lib.vmps_paged_decode_step(
+            _ptr(out), _ptr(q), q.stride(0), _ptr(k), ks, _ptr(v), vs, _ptr(positions),
+            _ptr(slot_mapping), _ptr(inv_freq), _ptr(pool), _ptr(block_tables),
+            block_tables.shape[1], _ptr(seq_lens), B, n_q, n_kv, D, block_size, num_blocks,
+            float(scale), _ptr(ws), ws.numel() * ws.element_size(), dtype_code(pool.dtype),
+            _stream(dev))
+    _check(rc, "paged_decode_step")
+    return out
+
+
+def error_word(device: torch.device | int | None = None) -> int:
+    """Read and clear the device error word (bit meanings in include/vmps.h)."""
+    dev = torch.device("cuda", device) if isinstance(device, int) else (device or torch.device("cuda"))
+    word = ctypes.c_int(0)
+    lib = load_library()
+    with torch.cuda.device(dev):
+        _check(lib.vmps_debug_error_word(_stream(dev), ctypes.byref(word)), "debug_error_word")
+    return word.value
+
+
+# ── reference-named entry points (kernels/__init__.py) ───────────────────────
+
+
+def fused_attention(pool: torch.Tensor, new_k: torch.Tensor, new_v: torch.Tensor,
+                    queries: torch.Tensor, bt_tensor: torch.Tensor, sl_tensor: torch.Tensor,
+                    write_info: torch.Tensor, n_heads: int, n_kv_heads: int, d_k: int,
+                    block_size: int) -> torch.Tensor:
+    """Write the new (already rotated) K/V, then attend; returns (B, n_heads, d_k).
+
+    Same contract as the reference's ``fused_attention_metal_fast``
+    (kernels/__init__.py:320-368): ``write_info`` is int32 (B, 2) of
+    (block_id, token_pos), ``sl_tensor`` counts the new token, ``bt_tensor``
+    is the zero-padded int32 (B, max_blocks) block table.  The write and the
+    attention are two launches on one stream, so the new token is always
+    visible to the attention (the Metal kernel relied on redundant
+    per-threadgroup writes instead, kernels/__init__.py:135-164).
+    """
+    B = queries.shape[0]
+    if pool.shape[3] != n_kv_heads or pool.shape[4] != d_k or pool.shape[2] != block_size:
+        raise ValueError("pool shape does not match n_kv_heads / d_k / block_size")
+    if queries.shape[1:] != (n_heads, d_k):
+        raise ValueError("queries must be (B, n_heads, d_k)")
+    _int32(write_info, "write_info")
+    slot = (write_info[:, 0] * block_size + write_info[:, 1]).to(torch.int32)
+    rope_reshape_and_cache(None, new_k.contiguous(), new_v.contiguous(), None, slot, None, pool)
+    return paged_decode_attention(queries.contiguous(), pool, bt_tensor, sl_tensor)
+
+
+#: The reference's name for the same entry point.
+fused_attention_metal_fast = fused_attention
+
+
+def gather_kv(pool: torch.Tensor, block_tables: torch.Tensor, seq_lens: torch.Tensor,
+              max_seq_len: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Padded paged gather ``(B, max_seq_len, n_kv, D)`` of K and V (zeros past seq_len).
+
+    API-compatible with ``gather_kv_metal`` (kernels/__init__.py:279-312).
+    Not on the decode hot path (the attention kernel reads pages in place);
+    implemented with device-side indexing.
+    """
+    _require_cuda(pool, block_tables, seq_lens)
+    num_blocks, bs, n_kv, D = _check_pool(pool)
+    B = block_tables.shape[0]
+    t = torch.arange(max_seq_len, device=pool.device)
+    page = (t // bs).clamp_max(block_tables.shape[1] - 1)
+    blk = block_tables.long().gather(1, page.unsqueeze(0).expand(B, -1))
+    off = (t % bs).unsqueeze(0).expand(B, -1)
+    k = pool[blk, 0, off]
+    v = pool[blk, 1, off]
+    valid = (t.unsqueeze(0) < seq_lens.long().unsqueeze(1)).unsqueeze(-1).unsqueeze(-1)
+    return k * valid, v * valid
