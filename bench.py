@@ -1,0 +1,485 @@
+#!/usr/bin/env python
+"""Throughput of the paged decode-attention step on B200 (one JSON line on stdout).
+
+Workload (config 1 of the north star, the single-GPU microbench): one decode
+step of one attention layer for a batch of 64 sequences -- 32 query heads,
+4 kv heads, head_dim 64, fp16, context lengths uniform in [1, 2048], block
+tables a random permutation of a 16384-block pool.  A "step" is the hot path
+of ``PagedAttentionLayer._forward_batch`` between its projections: RoPE on
+Q/K, the K/V write into the pool slot, and paged GQA decode attention
+(``vmps_paged_decode_step`` = kernel 1 + kernel 2 + the split-K combine).
+
+Sequences are independent, so ``--gpus N`` shards them: every rank runs its
+own 64-sequence batch on its own pool (weak scaling, no collective on the
+data path; one all-reduce after the timed region takes the max time).
+
+Measurement:
+* ``value``: tokens/s of the whole job, inputs resident in HBM, CUDA-graph
+  replays of the step timed with CUDA events (max over ranks).  Eight pool
+  replicas (8 x 256 MiB, 8 x ~67 MB touched) are rotated so successive steps
+  never hit in the 126 MB L2.
+* ``e2e``: the same metric through the public Python API
+  (``vllm_mps_b200.kernels.paged_decode_step``) with the per-step inputs in
+  pinned host memory, copied to the device, and the output copied back,
+  inside the timed region.  The KV pool is device-resident state.
+* ``roofline``: the attention kernel (+ its combine) timed alone with CUDA
+  events; algorithmic bytes = K/V rows read + q + out + block-table entries
+  + seq_lens; peak = measured HBM copy bandwidth (MEASURED_PEAKS.json).
+* ``cpu_baseline``: the C oracle (oracle/vmps_oracle.c, a port of the
+  reference's CPU path) on the host cores, rank 0, N=1 only.
+
+``--impl reference`` times that CPU implementation alone (the reference is
+Python + Metal; its CPU path is what runs off Apple hardware).
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: (B, n_q, n_kv, D, dtype, ctx_lo, ctx_hi, num_blocks, replicas, description)
+    "c1": (64, 32, 4, 64, "float16", 1, 2048, 16384, 8,
+           "C1 single-layer paged decode step: batch 64, 32 q / 4 kv heads, head_dim 64, "
+           "fp16, ctx U[1,2048], block_size 16, permuted 16384-block pool"),
+    "c3": (4, 64, 8, 128, "float16", 131072, 131072, 32768 + 64, 2,
+           "C3 long-context split-K decode: batch 4 x 131072, 64 q / 8 kv heads, "
+           "head_dim 128, fp16, permuted 32832-block pool"),
+}
+BLOCK = 16
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(cfg_name):
+    """DRAM bytes per launch of the attention kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", f"paged_decode_{cfg_name}.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+def make_host_workload(cfg, seed):
+    B, n_q, n_kv, D, dt, lo, hi, nb, R, _ = cfg
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(lo, hi + 1, size=B).astype(np.int64)
+    pages = (ctx + BLOCK - 1) // BLOCK
+    maxb = int(pages.max())
+    tables = []
+    for _ in range(R):
+        perm = rng.permutation(nb)
+        bt = np.zeros((B, maxb), np.int32)
+        off = 0
+        for i, p in enumerate(pages):
+            bt[i, :p] = perm[off:off + p]
+            off += p
+        tables.append(bt)
+    return ctx, pages, tables
+
+
+def alg_bytes(cfg, ctx, pages):
+    B, n_q, n_kv, D = cfg[0], cfg[1], cfg[2], cfg[3]
+    kv = int(ctx.sum()) * n_kv * D * 2 * 2
+    return kv + 2 * B * n_q * D * 2 + int(pages.sum()) * 4 + 4 * B
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons with NVML while running."""
+
+    NAMES = {
+        "nvmlClocksEventReasonGpuIdle": "gpu_idle",
+        "nvmlClocksEventReasonApplicationsClocksSetting": "applications_clocks_setting",
+        "nvmlClocksEventReasonSwPowerCap": "sw_power_cap",
+        "nvmlClocksEventReasonHwSlowdown": "hw_slowdown",
+        "nvmlClocksEventReasonSyncBoost": "sync_boost",
+        "nvmlClocksEventReasonSwThermalSlowdown": "sw_thermal_slowdown",
+        "nvmlClocksEventReasonHwThermalSlowdown": "hw_thermal_slowdown",
+        "nvmlClocksEventReasonHwPowerBrakeSlowdown": "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, index, period=0.01):
+        self.samples, self.reasons, self.ok = [], set(), False
+        self.period = period
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # no NVML: report nulls
+            log(f"clock sampling unavailable: {e}")
+            self.max_mhz = None
+
+    def _sample(self):
+        nv = self.nv
+        self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+        mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        for attr, name in self.NAMES.items():
+            if mask & getattr(nv, attr, 0):
+                self.reasons.add(name)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._sample()
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+            try:
+                self._sample()
+            except Exception:
+                pass
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": []}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+def cpu_baseline(cfg, ctx, tables, budget_s=10.0):
+    """C oracle (port of the reference's CPU path) on all host cores, bounded sample."""
+    from oracle import c_oracle
+    from oracle.paged_attention_oracle import f32_to_bits, rope_inv_freq
+
+    c_oracle.build()
+    B, n_q, n_kv, D, dt, lo, hi, nb, R, _ = cfg
+    rng = np.random.default_rng(99)
+    pool = f32_to_bits(rng.standard_normal((nb, 2, BLOCK, n_kv, D), dtype=np.float32), dt)
+    q = f32_to_bits(rng.standard_normal((B, n_q, D), dtype=np.float32), dt)
+    k = f32_to_bits(rng.standard_normal((B, n_kv, D), dtype=np.float32), dt)
+    v = f32_to_bits(rng.standard_normal((B, n_kv, D), dtype=np.float32), dt)
+    inv = rope_inv_freq(D, 10000.0)
+    threads = os.cpu_count() or 1
+    # Warm-up, then as many full steps as fit in the budget (at least one).
+    c_oracle.decode_step(q, k, v, ctx - 1, ctx, tables[0], pool, inv, dt, threads=threads)
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        c_oracle.decode_step(q, k, v, ctx - 1, ctx, tables[n % len(tables)], pool, inv, dt,
+                             threads=threads)
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt_s = time.perf_counter() - t0
+    return {"value": B * n / dt_s, "unit": "tokens/s", "cores": c_oracle.max_threads(),
+            "kind": "port",
+            "sample": f"{n} full steps of the same workload ({B} seqs, sum ctx {int(ctx.sum())}) "
+                      f"in {dt_s:.1f} s, C oracle (oracle/vmps_oracle.c), OpenMP"}
+
+
+def run_reference(args, cfg, rank, world):
+    if rank != 0:
+        return 0
+    from oracle import c_oracle
+    from oracle.paged_attention_oracle import f32_to_bits, rope_inv_freq
+
+    c_oracle.build()
+    B, n_q, n_kv, D, dt, lo, hi, nb, R, desc = cfg
+    ctx, pages, tables = make_host_workload(cfg, seed=1000)
+    rng = np.random.default_rng(99)
+    pool = f32_to_bits(rng.standard_normal((nb, 2, BLOCK, n_kv, D), dtype=np.float32), dt)
+    q = f32_to_bits(rng.standard_normal((B, n_q, D), dtype=np.float32), dt)
+    k = f32_to_bits(rng.standard_normal((B, n_kv, D), dtype=np.float32), dt)
+    v = f32_to_bits(rng.standard_normal((B, n_kv, D), dtype=np.float32), dt)
+    inv = rope_inv_freq(D, 10000.0)
+    threads = os.cpu_count() or 1
+
+    def step(i, sel):
+        c_oracle.decode_step(q[sel], k[sel], v[sel], ctx[sel] - 1, ctx[sel], tables[i % R][sel],
+                             pool, inv, dt, threads=threads)
+
+    # Size the per-step sample so the whole run stays within ~3 minutes.
+    full = np.arange(B)
+    t0 = time.perf_counter()
+    step(0, full)
+    t_full = time.perf_counter() - t0
+    total = args.steps + args.warmup
+    budget = 150.0
+    sel = full
+    if t_full * total > budget:
+        keep = max(1, int(B * budget / (t_full * total)))
+        sel = np.sort(np.random.default_rng(5).choice(B, size=keep, replace=False))
+    for i in range(args.warmup):
+        step(i, sel)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(i, sel)
+    el = time.perf_counter() - t0
+    toks = len(sel) * args.steps
+    val = toks / el
+    line = {
+        "metric": "decode tokens/s", "value": val, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded)", "impl": "reference",
+        "config": {"workload": desc, "global_batch": B, "parallelism": "host cores"},
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": c_oracle.max_threads(),
+                         "kind": "port",
+                         "sample": f"{len(sel)} of {B} sequences per step (sum ctx "
+                                   f"{int(ctx[sel].sum())}), C oracle oracle/vmps_oracle.c"},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, cfg, rank, world, local_rank):
+    import torch
+
+    from vllm_mps_b200 import kernels as K
+    from vllm_mps_b200.layers.rotary_embedding import rope_inv_freq
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, n_q, n_kv, D, dt, lo, hi, nb, R, desc = cfg
+    tdt = getattr(torch, dt)
+    ctx, pages, tables = make_host_workload(cfg, seed=1000 + rank)
+    maxb = tables[0].shape[1]
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    pools = [torch.randn((nb, 2, BLOCK, n_kv, D), generator=g, device=dev, dtype=torch.float32)
+             .to(tdt) for _ in range(R)]
+    qs = [torch.randn((B, n_q, D), generator=g, device=dev, dtype=torch.float32).to(tdt)
+          for _ in range(R)]
+    k = torch.randn((B, n_kv, D), generator=g, device=dev, dtype=torch.float32).to(tdt)
+    v = torch.randn((B, n_kv, D), generator=g, device=dev, dtype=torch.float32).to(tdt)
+    pos_np = (ctx - 1).astype(np.int32)
+    pos = torch.from_numpy(pos_np).to(dev)
+    sl = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+    bts = [torch.from_numpy(t).to(dev) for t in tables]
+    slots_np = [np.array([t[i, p // BLOCK] * BLOCK + p % BLOCK for i, p in enumerate(pos_np)],
+                         np.int32) for t in tables]
+    slots = [torch.from_numpy(s).to(dev) for s in slots_np]
+    inv = rope_inv_freq(D, 10000.0).to(dev)
+    outs = [torch.empty((B, n_q, D), dtype=tdt, device=dev) for _ in range(R)]
+    ws = K.DecodeWorkspace()
+
+    def step(r):
+        K.paged_decode_step(qs[r], k, v, pos, slots[r], inv, pools[r], bts[r], sl,
+                            out=outs[r], workspace=ws)
+
+    def attn(r):
+        K.paged_decode_attention(qs[r], pools[r], bts[r], sl, out=outs[r], workspace=ws)
+
+    # Eager warm-up (loads the library, sizes the workspace), then capture one
+    # graph per replica for the step and for the attention kernel alone.
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for r in range(R):
+            step(r)
+            attn(r)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    g_step, g_attn = [], []
+    for r in range(R):
+        gs = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gs):
+            step(r)
+        ga = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(ga):
+            attn(r)
+        g_step.append(gs)
+        g_attn.append(ga)
+    torch.cuda.synchronize(dev)
+    if K.error_word(dev):
+        raise RuntimeError("device error word set during warm-up")
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ── timed region: K steps ────────────────────────────────────────────────
+    for i in range(args.warmup):
+        g_step[i % R].replay()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clocks:
+        e0.record()
+        for i in range(args.steps):
+            g_step[i % R].replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+    barrier()
+    t_step = max_over_ranks(e0.elapsed_time(e1) * 1e-3)
+
+    # ── the attention kernel alone (roofline) ──────────────────────────────────
+    n_k = max(args.steps, 20)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n_k)]
+    for i in range(max(args.warmup, 3)):
+        g_attn[i % R].replay()
+    torch.cuda.synchronize(dev)
+    for i in range(n_k):
+        evs[i][0].record()
+        g_attn[i % R].replay()
+        evs[i][1].record()
+    torch.cuda.synchronize(dev)
+    t_kernel = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in evs) * 1e-3)
+
+    # ── end to end through the public API with host buffers ───────────────────
+    hq = [qs[r].cpu().pin_memory() for r in range(R)]
+    hk, hv = k.cpu().pin_memory(), v.cpu().pin_memory()
+    hpos = torch.from_numpy(pos_np).pin_memory()
+    hsl = torch.from_numpy(ctx.astype(np.int32)).pin_memory()
+    hbt = [torch.from_numpy(t).pin_memory() for t in tables]
+    hslot = [torch.from_numpy(s).pin_memory() for s in slots_np]
+    hout = torch.empty((B, n_q, D), dtype=tdt).pin_memory()
+    dq = torch.empty_like(qs[0])
+    dk, dv = torch.empty_like(k), torch.empty_like(v)
+    dpos, dsl = torch.empty_like(pos), torch.empty_like(sl)
+    dbt = torch.empty_like(bts[0])
+    dslot = torch.empty_like(slots[0])
+    h2d = sum(t.numel() * t.element_size() for t in (hq[0], hk, hv, hpos, hsl, hbt[0], hslot[0]))
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step(i):
+        r = i % R
+        dq.copy_(hq[r], non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        dpos.copy_(hpos, non_blocking=True)
+        dsl.copy_(hsl, non_blocking=True)
+        dbt.copy_(hbt[r], non_blocking=True)
+        dslot.copy_(hslot[r], non_blocking=True)
+        out = K.paged_decode_step(dq, dk, dv, dpos, dslot, inv, pools[r], dbt, dsl, workspace=ws)
+        hout.copy_(out, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for i in range(args.steps):
+        e2e_step(i)
+    e3.record()
+    torch.cuda.synchronize(dev)
+    barrier()
+    t_e2e = max_over_ranks(e2.elapsed_time(e3) * 1e-3)
+    err = K.error_word(dev)
+    if err:
+        raise RuntimeError(f"device error word {err} after the timed regions")
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        ab = alg_bytes(cfg, ctx, pages)
+        achieved = ab / t_kernel / 1e9
+        line = {
+            "metric": "decode tokens/s", "value": world * B * args.steps / t_step,
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t_step / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded N(0,1) q/k/v/pool; seeded ragged contexts)",
+            "config": {
+                "workload": desc, "global_batch": B * world, "seq_len": "U[%d,%d]" % (lo, hi),
+                "sum_ctx_per_rank": int(ctx.sum()), "parallelism": f"sequence-sharded x{world}",
+                "l2": f"inputs larger than L2: {R} pool/table replicas rotated "
+                      f"({R} x {ab / 1e6:.0f} MB touched per cycle)",
+                "timing": "CUDA graph replay per step, CUDA events, max over ranks",
+            },
+            "e2e": {"value": world * B * args.steps / t_e2e, "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "vllm_mps_b200.kernels.paged_decode_step, pinned host inputs"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": profile_traffic(args.config),
+                         "peak_kind": peak_kind, "kernel": "paged_decode_kernel + combine",
+                         "kernel_us": t_kernel * 1e6, "alg_bytes_per_launch": ab},
+            "clocks": clocks.summary(),
+            "gpu_launches": 3 * args.steps,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(cfg, ctx, tables)
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    cfg = CONFIGS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, cfg, rank, world)
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        return run_ours(args, cfg, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

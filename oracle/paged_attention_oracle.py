@@ -51,7 +51,8 @@ def f32_to_bits(x: np.ndarray, dtype: str) -> np.ndarray:
     """float32 -> raw uint16 of ``dtype`` with round-to-nearest-even."""
     x = np.asarray(x, dtype=np.float32)
     if dtype == "float16":
-        return x.astype(np.float16).view(np.uint16)
+        with np.errstate(over="ignore"):  # out-of-range values round to inf, as in torch
+            return x.astype(np.float16).view(np.uint16)
     if dtype == "bfloat16":
         u = x.view(np.uint32).astype(np.uint64)
         nan = np.isnan(x)
