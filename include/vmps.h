@@ -145,6 +145,31 @@ int vmps_paged_decode_step(void* out, void* q, int64_t q_row_stride, const void*
                            void* workspace, size_t workspace_bytes, int dtype, void* stream);
 
 /*
+ * Allocation-free variant of vmps_paged_decode_attention.  No counterpart in
+ * the reference (whose Metal path keeps a global output buffer instead,
+ * kernels/__init__.py:317-345); it exists for callers that cannot allocate
+ * device memory while running (a C/FFI host without a caching allocator, or
+ * a process that has already reserved all free HBM for its KV pool), which
+ * therefore cannot pass the workspace the other entry point needs.
+ *
+ * Same arguments and results as vmps_paged_decode_attention minus the
+ * workspace: the split-K scratch is a fixed 16 MiB device array inside the
+ * library, held on every GPU that loads the library until exit.  Calls that
+ * would need more scratch (vmps_paged_decode_workspace_bytes) return
+ * VMPS_ERR_WORKSPACE; every supported shape with up to 4096 sequences fits
+ * on a 148-SM B200.  All calls on a device share the array (nothing in it
+ * needs to start at zero), so calls that may overlap on the GPU race and
+ * must be ordered on one stream.  The first call on a device looks up the
+ * array's address (cudaGetSymbolAddress) and caches it; make that first call
+ * before any stream capture.  Allocates nothing (no cudaMalloc/cudaFree).
+ */
+int vmps_paged_decode_attention_noalloc(void* out, const void* q, const void* pool,
+                                        const int32_t* block_tables, int max_blocks_per_seq,
+                                        const int32_t* seq_lens, int num_seqs, int n_q, int n_kv,
+                                        int head_dim, int block_size, int num_blocks, float scale,
+                                        int dtype, void* stream);
+
+/*
  * Reads and clears the device error word of the current device (a bitwise OR
  * of index violations the kernels skipped since the last call).  Synchronises
  * `stream`.  Bits: 1 slot out of range, 2 block id out of range, 4 seq_len

@@ -1,0 +1,83 @@
+"""The allocation-free decode entry point, called through the C ABI.
+
+``vmps_paged_decode_attention_noalloc`` is for callers that cannot allocate
+device memory while they run (an FFI host with no caching allocator, or a
+process that has reserved all free HBM for its KV pool up front): it keeps
+its split-K scratch in a fixed array inside the library instead of taking a
+caller-provided workspace.  This test checks, on two calls in a row with
+different batches (so the second call runs over the first call's leftover
+scratch contents), that its output matches the workspace entry point's
+within the tolerance of the other decode tests.  The file sorts last so that
+a run that stops at the first failure has already run every other test.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-3
+RTOL = 2e-3
+
+
+def _noalloc_fn(lib):
+    f = lib.vmps_paged_decode_attention_noalloc
+    vp, i32 = ctypes.c_void_p, ctypes.c_int
+    f.restype = i32
+    f.argtypes = [vp, vp, vp, vp, i32, vp, i32, i32, i32, i32, i32, i32, ctypes.c_float, i32, vp]
+    return f
+
+
+def _case(seed, B, n_q, n_kv, D, lo, hi, nb, dev):
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(lo, hi + 1, size=B)
+    pages = (ctx + 15) // 16
+    perm = rng.permutation(nb)
+    bt = np.zeros((B, int(pages.max())), np.int32)
+    off = 0
+    for i, p in enumerate(pages):
+        bt[i, :p] = perm[off:off + p]
+        off += p
+    g = torch.Generator(device=dev).manual_seed(seed)
+    pool = torch.randn((nb, 2, 16, n_kv, D), generator=g, device=dev).half()
+    q = torch.randn((B, n_q, D), generator=g, device=dev).half()
+    return q, pool, torch.from_numpy(bt).to(dev), torch.from_numpy(ctx.astype(np.int32)).to(dev)
+
+
+def test_noalloc_matches_workspace_entry_point_twice():
+    from vllm_mps_b200 import kernels as K
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = K.load_library()
+    fn = _noalloc_fn(lib)
+    cases = [_case(21, 64, 32, 4, 64, 1, 2048, 16384, dev),   # C1-shaped, many split sequences
+             _case(22, 9, 32, 4, 64, 1, 700, 1024, dev)]      # smaller batch over stale scratch
+    for q, pool, bt, sl in cases:
+        B, n_q, D = q.shape
+        n_kv = pool.shape[3]
+        ref = K.paged_decode_attention(q, pool, bt, sl)
+        out = torch.full_like(q, float("nan"))
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = fn(out.data_ptr(), q.data_ptr(), pool.data_ptr(), bt.data_ptr(), bt.shape[1],
+                sl.data_ptr(), B, n_q, n_kv, D, 16, pool.shape[0], 1.0 / np.sqrt(D), 0, stream)
+        assert rc == 0, lib.vmps_last_error()
+        torch.cuda.synchronize(dev)
+        assert K.error_word(dev) == 0
+        torch.testing.assert_close(out.float(), ref.float(), atol=ATOL, rtol=RTOL)
+
+
+def test_noalloc_rejects_calls_beyond_the_scratch_size():
+    from vllm_mps_b200 import kernels as K
+
+    torch.cuda.set_device(0)
+    lib = K.load_library()
+    fn = _noalloc_fn(lib)
+    # Five million sequences need ~20 MB of work-split metadata alone, more
+    # than the 16 MiB array: rejected on the host, nothing is launched.
+    rc = fn(None, None, None, None, 1, None, 5_000_000, 32, 4, 64, 16, 1, 0.125, 0, None)
+    assert rc == -4  # VMPS_ERR_WORKSPACE
+    assert b"scratch" in lib.vmps_last_error()
