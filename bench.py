@@ -7,7 +7,7 @@ step of one attention layer for a batch of 64 sequences -- 32 query heads,
 tables a random permutation of a 16384-block pool.  A "step" is the hot path
 of ``PagedAttentionLayer._forward_batch`` between its projections: RoPE on
 Q/K, the K/V write into the pool slot, and paged GQA decode attention
-(``vmps_paged_decode_step`` = kernel 1 + kernel 2 + the split-K combine).
+(``vmps_paged_decode_step``: one kernel launch per step).
 
 Sequences are independent, so ``--gpus N`` shards them: every rank runs its
 own 64-sequence batch on its own pool (weak scaling, no collective on the
@@ -22,9 +22,9 @@ Measurement:
   (``vllm_mps_b200.kernels.paged_decode_step``) with the per-step inputs in
   pinned host memory, copied to the device, and the output copied back,
   inside the timed region.  The KV pool is device-resident state.
-* ``roofline``: the attention kernel (+ its combine) timed alone with CUDA
-  events; algorithmic bytes = K/V rows read + q + out + block-table entries
-  + seq_lens; peak = measured HBM copy bandwidth (MEASURED_PEAKS.json).
+* ``roofline``: the attention kernel timed alone with CUDA events (graphs of
+  8 launches); algorithmic bytes = K/V rows read + q + out + block-table
+  entries + seq_lens; peak = measured HBM copy bandwidth (MEASURED_PEAKS.json).
 * ``cpu_baseline``: the C oracle (oracle/vmps_oracle.c, a port of the
   reference's CPU path) on the host cores, rank 0, N=1 only.
 
@@ -304,8 +304,10 @@ def run_ours(args, cfg, rank, world, local_rank):
     def attn(r):
         K.paged_decode_attention(qs[r], pools[r], bts[r], sl, out=outs[r], workspace=ws)
 
-    # Eager warm-up (loads the library, sizes the workspace), then capture one
-    # graph per replica for the step and for the attention kernel alone.
+    # Eager warm-up (loads the library, sizes the workspace), then capture the
+    # steps as CUDA graphs: one graph of R consecutive steps (one per replica,
+    # chained with programmatic dependent launch, as a serving loop would
+    # replay them) and single-step graphs for a remainder of K % R steps.
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
@@ -314,17 +316,24 @@ def run_ours(args, cfg, rank, world, local_rank):
             attn(r)
     torch.cuda.current_stream(dev).wait_stream(side)
     torch.cuda.synchronize(dev)
-    g_step, g_attn = [], []
-    for r in range(R):
-        gs = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gs):
-            step(r)
-        ga = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(ga):
-            attn(r)
-        g_step.append(gs)
-        g_attn.append(ga)
+
+    def capture(fn_list):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for fn in fn_list:
+                fn()
+        return gr
+
+    g_steps = capture([lambda r=r: step(r) for r in range(R)])
+    g_step1 = [capture([lambda r=r: step(r)]) for r in range(R)]
+    g_attns = capture([lambda r=r: attn(r) for r in range(R)])
     torch.cuda.synchronize(dev)
+
+    def run_steps(n):
+        for _ in range(n // R):
+            g_steps.replay()
+        for r in range(n % R):
+            g_step1[r].replay()
     if K.error_word(dev):
         raise RuntimeError("device error word set during warm-up")
 
@@ -345,32 +354,31 @@ def run_ours(args, cfg, rank, world, local_rank):
         return float(t.item())
 
     # ── timed region: K steps ────────────────────────────────────────────────
-    for i in range(args.warmup):
-        g_step[i % R].replay()
+    run_steps(args.warmup)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index if dev.index is not None else 0) as clocks:
         e0.record()
-        for i in range(args.steps):
-            g_step[i % R].replay()
+        run_steps(args.steps)
         e1.record()
         torch.cuda.synchronize(dev)
     barrier()
     t_step = max_over_ranks(e0.elapsed_time(e1) * 1e-3)
 
-    # ── the attention kernel alone (roofline) ──────────────────────────────────
-    n_k = max(args.steps, 20)
+    # ── the attention kernel alone (roofline): R launches per graph replay,
+    # CUDA events around every replay; duration per launch = replay time / R.
+    n_k = max(args.steps // R, 20)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(n_k)]
-    for i in range(max(args.warmup, 3)):
-        g_attn[i % R].replay()
+    for _ in range(max(args.warmup // R, 3)):
+        g_attns.replay()
     torch.cuda.synchronize(dev)
     for i in range(n_k):
         evs[i][0].record()
-        g_attn[i % R].replay()
+        g_attns.replay()
         evs[i][1].record()
     torch.cuda.synchronize(dev)
-    t_kernel = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in evs) * 1e-3)
+    t_kernel = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in evs) * 1e-3 / R)
 
     # ── end to end through the public API with host buffers ───────────────────
     hq = [qs[r].cpu().pin_memory() for r in range(R)]
@@ -430,17 +438,17 @@ def run_ours(args, cfg, rank, world, local_rank):
                 "sum_ctx_per_rank": int(ctx.sum()), "parallelism": f"sequence-sharded x{world}",
                 "l2": f"inputs larger than L2: {R} pool/table replicas rotated "
                       f"({R} x {ab / 1e6:.0f} MB touched per cycle)",
-                "timing": "CUDA graph replay per step, CUDA events, max over ranks",
+                "timing": f"CUDA graphs of {R} steps (PDL-chained), CUDA events, max over ranks",
             },
             "e2e": {"value": world * B * args.steps / t_e2e, "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "vllm_mps_b200.kernels.paged_decode_step, pinned host inputs"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profile_traffic(args.config),
-                         "peak_kind": peak_kind, "kernel": "paged_decode_kernel + combine",
+                         "peak_kind": peak_kind, "kernel": "paged_decode_kernel (attention only)",
                          "kernel_us": t_kernel * 1e6, "alg_bytes_per_launch": ab},
             "clocks": clocks.summary(),
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": args.steps,
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(cfg, ctx, tables)

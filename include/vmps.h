@@ -82,17 +82,20 @@ int vmps_rope_reshape_and_cache(void* q_out, const void* q, int64_t q_row_stride
                                 int num_blocks, int dtype, void* stream);
 
 /*
- * Workspace needed by vmps_paged_decode_attention on the current device for
- * up to `num_seqs` sequences (the split-K partial results of sequences cut
- * between CTAs, and the work split the combine step reads).  Its contents
- * need no initialisation; calls sharing a workspace must be ordered (same
- * stream).  Returns 0 if the shape is unsupported.
+ * Workspace needed by vmps_paged_decode_attention / vmps_paged_decode_step
+ * on the current device for up to `num_seqs` sequences: split-K partial
+ * results of sequences cut between CTAs, and one arrival counter per kv head
+ * and sequence (a fixed 1 MiB region, so one workspace serves calls of any
+ * shape).  The workspace must be zero-filled once after allocation
+ * (vmps_paged_decode_workspace_init); every call leaves the counters at zero
+ * again.  Calls sharing a workspace must be ordered (same stream).  Returns 0
+ * if the shape is unsupported.
  */
 size_t vmps_paged_decode_workspace_bytes(int num_seqs, int n_q, int n_kv, int head_dim,
                                          int dtype);
 
-/* cudaMemsetAsync(workspace, 0, bytes, stream); optional (kept for callers
- * that want a deterministic initial state). */
+/* cudaMemsetAsync(workspace, 0, bytes, stream): the one-time initialisation
+ * a new workspace needs. */
 int vmps_paged_decode_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
 
 /*
@@ -113,10 +116,10 @@ int vmps_paged_decode_workspace_init(void* workspace, size_t workspace_bytes, vo
  * sequence with seq_len 0 gets a zero output row.
  *
  * Supported: head_dim 64 or 128, block_size 16, n_q / n_kv in {1,2,4,8,16},
- * num_seqs <= 4096.  Long sequences are split across CTAs (flash-decoding);
- * a second, small kernel merges the pieces.  Both are launched with
- * programmatic dependent launch (they wait for the preceding kernel's writes
- * before reading q or the pool).
+ * n_kv <= 64, num_seqs <= 4096.  Long sequences are split across CTAs (flash-decoding)
+ * and the last piece to finish merges them in the same launch.  The kernel
+ * is launched with programmatic dependent launch (it waits for the
+ * preceding kernel's writes before reading anything).
  */
 int vmps_paged_decode_attention(void* out, const void* q, const void* pool,
                                 const int32_t* block_tables, int max_blocks_per_seq,
@@ -125,16 +128,21 @@ int vmps_paged_decode_attention(void* out, const void* q, const void* pool,
                                 void* workspace, size_t workspace_bytes, int dtype, void* stream);
 
 /*
- * One decode step of one attention layer: kernel 1 then kernel 2 on `stream`.
+ * One decode step of one attention layer in a single kernel launch.
  *
- * Equivalent to vmps_rope_reshape_and_cache(q, q, ...) (Q rotated in place,
- * rotated K and V written to the pool) followed by
- * vmps_paged_decode_attention(out, q, ...), i.e. PagedAttentionLayer's
- * batched step between its projections (layers/paged_attention_layer.py:275-359)
- * and the whole Metal fused_attention shader (kernels/__init__.py:99-242)
- * with RoPE folded in.  Because the attention kernel knows its predecessor
- * only writes q and the pool, it reads seq_lens while kernel 1 is still
- * running.  q must be packed (q_row_stride == n_q * head_dim).
+ * Same result as vmps_rope_reshape_and_cache (rotated K and V written to
+ * the pool slot) followed by vmps_paged_decode_attention on the rotated q,
+ * i.e. PagedAttentionLayer's batched step between its projections
+ * (layers/paged_attention_layer.py:275-359) and the whole Metal
+ * fused_attention shader (kernels/__init__.py:99-242) with RoPE folded in.
+ * q is rotated in registers and left unchanged in memory.  Requirements:
+ * seq_lens[i] >= 1 and slot_mapping[i] addresses a slot of the last page of
+ * sequence i (as the reference's write_info always does for position
+ * seq_len-1); otherwise the write is flagged in the error word (bit 32).
+ * seq_lens are read before the preceding kernel on the stream finishes
+ * (programmatic dependent launch), so they must not be produced by that
+ * kernel; q/k/v/positions/slots/tables/pool are read after it finishes.
+ * q/k/v rows may have any row stride (slices of a fused QKV output).
  */
 int vmps_paged_decode_step(void* out, void* q, int64_t q_row_stride, const void* k,
                            int64_t k_row_stride, const void* v, int64_t v_row_stride,
@@ -153,14 +161,15 @@ int vmps_paged_decode_step(void* out, void* q, int64_t q_row_stride, const void*
  * therefore cannot pass the workspace the other entry point needs.
  *
  * Same arguments and results as vmps_paged_decode_attention minus the
- * workspace: the split-K scratch is a fixed 16 MiB device array inside the
+ * workspace: the split-K scratch is a fixed 8 MiB device array inside the
  * library, held on every GPU that loads the library until exit.  Calls that
  * would need more scratch (vmps_paged_decode_workspace_bytes) return
- * VMPS_ERR_WORKSPACE; every supported shape with up to 4096 sequences fits
- * on a 148-SM B200.  All calls on a device share the array (nothing in it
- * needs to start at zero), so calls that may overlap on the GPU race and
- * must be ordered on one stream.  The first call on a device looks up the
- * array's address (cudaGetSymbolAddress) and caches it; make that first call
+ * VMPS_ERR_WORKSPACE; on a 148-SM B200 every supported shape with up to 8
+ * query heads per kv head fits, 16 query heads per kv head does not.  All calls on a device share the array, so calls that
+ * may overlap on the GPU race and must be ordered on one stream.  The first
+ * call on a device looks up the array's address (cudaGetSymbolAddress),
+ * caches it and clears the array on the caller's stream (its merge counters
+ * must start at zero; every call leaves them at zero); make that first call
  * before any stream capture.  Allocates nothing (no cudaMalloc/cudaFree).
  */
 int vmps_paged_decode_attention_noalloc(void* out, const void* q, const void* pool,
@@ -173,7 +182,8 @@ int vmps_paged_decode_attention_noalloc(void* out, const void* q, const void* po
  * Reads and clears the device error word of the current device (a bitwise OR
  * of index violations the kernels skipped since the last call).  Synchronises
  * `stream`.  Bits: 1 slot out of range, 2 block id out of range, 4 seq_len
- * beyond the block table, 8 an internal wait timed out, 16 negative position.
+ * beyond the block table, 8 an internal wait timed out, 16 negative position,
+ * 32 a fused-step slot outside the sequence's last page.
  */
 int vmps_debug_error_word(void* stream, int* word_out);
 

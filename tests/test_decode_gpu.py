@@ -211,26 +211,60 @@ def test_full_size_configs(cuda_device, which):
     assert torch.equal(out.view(torch.int16), out2.view(torch.int16))
 
 
-def test_workspace_needs_no_init_and_step_matches_two_calls(cuda_device):
-    """A garbage-filled workspace gives the same bits; the fused step == kernel 1 + kernel 2."""
+def test_fused_step_matches_kernel1_then_kernel2(cuda_device):
+    """The one-launch step == kernel 1 + kernel 2, bit for bit; q is left unrotated."""
     from vllm_mps_b200 import kernels as K
     from vllm_mps_b200.layers.rotary_embedding import rope_inv_freq
 
-    c = _seeded_case(7, 8, 32, 4, 64, "float16", 500, 2000, 2048, cuda_device)
-    inv = rope_inv_freq(64, 10000.0).to(cuda_device)
-    pool0, q0 = c["pool"].clone(), c["q"].clone()
-    ref = _run_step(K, c["q"], c["k"], c["v"], c["pos"], c["slot"], inv, c["pool"], c["bt"], c["sl"])
-    pool_ref = c["pool"].clone()
-    ws = K.DecodeWorkspace()
-    buf = ws.get(cuda_device, 8, 32, 4, 64, torch.float16)
-    buf.fill_(0xFF)  # NaN patterns everywhere
-    q1, pool1 = q0.clone(), pool0.clone()
-    out = K.paged_decode_step(q1, c["k"], c["v"], c["pos"], c["slot"], inv, pool1, c["bt"],
-                              c["sl"], workspace=ws)
+    for dt, n_q, n_kv, D in (("float16", 32, 4, 64), ("bfloat16", 32, 8, 128),
+                             ("float16", 64, 4, 64)):
+        c = _seeded_case(7, 8, n_q, n_kv, D, dt, 1, 2000, 2048, cuda_device)
+        inv = rope_inv_freq(D, 10000.0).to(cuda_device)
+        pool0, q0 = c["pool"].clone(), c["q"].clone()
+        ref = _run_step(K, c["q"], c["k"], c["v"], c["pos"], c["slot"], inv, c["pool"], c["bt"],
+                        c["sl"])
+        q1, pool1 = q0.clone(), pool0.clone()
+        for _ in range(2):  # twice: the merge counters must be back at zero
+            out = K.paged_decode_step(q1, c["k"], c["v"], c["pos"], c["slot"], inv, pool1,
+                                      c["bt"], c["sl"])
+            torch.cuda.synchronize()
+            assert K.error_word(cuda_device) == 0
+            assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+            assert torch.equal(pool1.view(torch.int16), c["pool"].view(torch.int16))
+            assert torch.equal(q1.view(torch.int16), q0.view(torch.int16))
+
+
+def test_fused_step_strided_qkv_and_golden(cuda_device):
+    """Fused step on slices of one packed QKV row (the fused-projection layout)."""
+    from vllm_mps_b200 import kernels as K
+    from vllm_mps_b200.layers.rotary_embedding import rope_inv_freq
+
+    d = load_golden("attn_c3_small.npz")
+    dt = str(d["dtype"])
+    n_q, n_kv, D = int(d["n_q"]), int(d["n_kv"]), int(d["D"])
+    B = d["q"].shape[0]
+    pool = _t16(golden_pool_bits(d), dt, cuda_device)
+    qkv = torch.empty(B, (n_q + 2 * n_kv) * D, dtype=getattr(torch, dt), device=cuda_device)
+    qkv[:, : n_q * D] = _t16(d["q"], dt, cuda_device).reshape(B, -1)
+    qkv[:, n_q * D: (n_q + n_kv) * D] = _t16(d["k"], dt, cuda_device).reshape(B, -1)
+    qkv[:, (n_q + n_kv) * D:] = _t16(d["v"], dt, cuda_device).reshape(B, -1)
+    q = qkv[:, : n_q * D].view(B, n_q, D)
+    k = qkv[:, n_q * D: (n_q + n_kv) * D]
+    v = qkv[:, (n_q + n_kv) * D:]
+    slots = torch.from_numpy((d["slot_block"].astype(np.int64) * 16 + d["slot_off"])
+                             .astype(np.int32)).to(cuda_device)
+    out = K.paged_decode_step(q, k, v, torch.from_numpy(d["positions"]).to(cuda_device), slots,
+                              rope_inv_freq(D, float(d["theta"])).to(cuda_device), pool,
+                              torch.from_numpy(d["block_tables"]).to(cuda_device),
+                              torch.from_numpy(d["seq_lens"]).to(cuda_device))
     torch.cuda.synchronize()
-    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
-    assert torch.equal(pool1.view(torch.int16), pool_ref.view(torch.int16))
-    assert torch.equal(q1.view(torch.int16), c["q"].view(torch.int16))
+    assert K.error_word(cuda_device) == 0
+    pool_after = _bits(pool)
+    for i in range(B):
+        np.testing.assert_array_equal(pool_after[d["slot_block"][i], 0, d["slot_off"][i]], d["written_k"][i])
+        np.testing.assert_array_equal(pool_after[d["slot_block"][i], 1, d["slot_off"][i]], d["written_v"][i])
+    np.testing.assert_allclose(O.bits_to_f32(_bits(out), dt), O.bits_to_f32(d["attn_out"], dt),
+                               atol=ATOL, rtol=RTOL)
 
 
 def test_edge_lengths_and_empty(cuda_device):

@@ -71,13 +71,21 @@ def test_noalloc_matches_workspace_entry_point_twice():
 
 
 def test_noalloc_rejects_calls_beyond_the_scratch_size():
+    """16 query heads per kv head need ~10.8 MB of scratch on a 148-SM B200 (> 8 MiB)."""
     from vllm_mps_b200 import kernels as K
 
-    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
     lib = K.load_library()
     fn = _noalloc_fn(lib)
-    # Five million sequences need ~20 MB of work-split metadata alone, more
-    # than the 16 MiB array: rejected on the host, nothing is launched.
-    rc = fn(None, None, None, None, 1, None, 5_000_000, 32, 4, 64, 16, 1, 0.125, 0, None)
-    assert rc == -4  # VMPS_ERR_WORKSPACE
+    need = lib.vmps_paged_decode_workspace_bytes(8, 64, 4, 64, 0)
+    assert need > 8 << 20
+    q, pool, bt, sl = _case(23, 8, 64, 4, 64, 1, 300, 256, dev)
+    out = torch.zeros_like(q)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    rc = fn(out.data_ptr(), q.data_ptr(), pool.data_ptr(), bt.data_ptr(), bt.shape[1],
+            sl.data_ptr(), 8, 64, 4, 64, 16, pool.shape[0], 0.125, 0, stream)
+    assert rc == -4  # VMPS_ERR_WORKSPACE, rejected on the host
     assert b"scratch" in lib.vmps_last_error()
+    torch.cuda.synchronize(dev)
+    assert torch.count_nonzero(out) == 0  # nothing was launched

@@ -1,49 +1,89 @@
-// Kernel 2: paged decode attention (one query token per sequence), sm_100a.
+// Kernel 2: paged decode attention (one query token per sequence), sm_100a,
+// optionally fused with kernel 1's RoPE and K/V write (the whole decode step
+// of one layer in one launch).
 //
 // Replaces the gather/pad loop, the GQA repeat and the masked softmax
 // attention of PagedAttentionLayer._forward_batch
-// (layers/paged_attention_layer.py:326-359) and Phases 2-4 of the Metal
-// fused_attention shader (kernels/__init__.py:166-241).
+// (layers/paged_attention_layer.py:326-359) and the Metal fused_attention
+// shader (kernels/__init__.py:99-242); in fused mode also the RoPE loop and
+// the write_kv loop (:275-286, :317-324).
 //
 // Design (B200):
-//  * Work unit = one 16-token page of one head group of one sequence.  The
-//    units of all sequences are laid end to end and every CTA of a persistent
-//    grid (num_SMs x kCtasPerSm) takes one contiguous, equal share, so
-//    ragged context lengths still keep all SMs busy (flash-decoding with
-//    balanced splits).  A sequence cut between CTAs leaves fp32 partial
-//    results (running max, sum, unnormalised output) in the workspace and a
-//    small combine kernel merges them.  Both kernels are launched with
-//    programmatic dependent launch, so each one's prologue (page prefix sums,
-//    barrier set-up) overlaps the tail of the kernel before it.
+//  * Work unit = one 16-token page of one head group (HPC kv heads, 16 KiB of
+//    K+V) of one sequence.  The units of all sequences are laid end to end and
+//    every CTA of a persistent grid takes one contiguous, equal share, so
+//    ragged batches and single long sequences both keep every SM streaming
+//    (flash-decoding with balanced splits).
 //  * A producer warp streams pages with the tiled TMA (cp.async.bulk.tensor,
-//    no multicast) into a 4-stage shared-memory ring guarded by mbarriers.
-//    The box is [64 d][16 tokens][HPC heads][K,V] with the 128-byte swizzle,
-//    so K and V of HPC kv heads arrive in one instruction per 64 columns.
+//    no multicast) into a shared-memory ring guarded by mbarriers.  The box
+//    is [64 d][16 tokens][HPC heads][K,V] with the 128-byte swizzle, so K and
+//    V of HPC kv heads arrive in one instruction per 64 columns.
 //  * One consumer warp per kv head.  The G query heads of a kv head are the
 //    N=8 side of the tensor-core MMA, so K and V are read once for the whole
 //    group and GQA is never materialised:
 //        S^T[16 tok x 8 heads] = K[16 x D] . Q^T[D x 8]        (mma.m16n8k16)
 //        online softmax over tokens per head (warp shuffles, fp32, exp2)
 //        O^T[D x 8]          += V^T[D x 16] . P^T[16 x 8]     (P via movmatrix)
-//  * Scores, softmax state and accumulators are fp32; the output is rounded
-//    once to the model dtype.
+//  * Fused mode: each warp rotates its Q fragments in registers, and the
+//    warp that owns a sequence's last page rotates the new K, writes K and V
+//    to the pool slot and patches them into its shared-memory copy of the
+//    page (no other CTA reads that page in this launch).  RoPE uses the
+//    reference's 16-bit rounding points, so the written K is bit-identical
+//    to kernel 1's.
+//  * A sequence cut between CTAs: every piece stores its fp32 state (running
+//    max, sum, unnormalised output in MMA-fragment order) and arrives on an
+//    atomic counter per kv head and sequence (release fence + relaxed add,
+//    issued a couple of pages later so it never stalls the page pipeline).
+//    The last piece to arrive stages all pieces into the freed shared-memory
+//    ring with cp.async (one round trip) and merges them.  Nobody waits on
+//    anybody.
+//  * The per-segment inputs of a CTA's first segments (query rows, new K/V,
+//    lengths, slots, RoPE tables) are staged in shared memory at the start,
+//    so a segment switch never waits on a global load queued behind the page
+//    stream.
+//  * Launched with programmatic dependent launch: in the fused step the
+//    prologue (page prefix sums, the first block-table entries, the first
+//    RoPE table) runs while the previous kernel in the stream finishes.
 #include <mutex>
 #include <utility>
 
 #include "vmps_abi_internal.h"
 #include "vmps_common.cuh"
 
+#ifndef VMPS_DECODE_STAGES
+#define VMPS_DECODE_STAGES 4
+#endif
+#ifndef VMPS_DECODE_CTAS_PER_SM
+#define VMPS_DECODE_CTAS_PER_SM 2
+#endif
+
 namespace vmps {
 
-constexpr int kStages = 4;
-constexpr int kCtasPerSm = 3;
+constexpr int kStages = VMPS_DECODE_STAGES;
+constexpr int kCtasPerSm = VMPS_DECODE_CTAS_PER_SM;
 constexpr int kMinPagesPerCta = 4;
 constexpr int kMaxSeqs = 4096;
+constexpr int kMaxKvHeads = 64;
+#ifndef VMPS_DECODE_SEG_TABLES
+#define VMPS_DECODE_SEG_TABLES 4
+#endif
+// Segments per CTA whose inputs (RoPE table, query rows, new K/V) are staged
+// in shared memory up front; later segments read them from global memory.
+constexpr int kSegTables = VMPS_DECODE_SEG_TABLES;
 constexpr int kPageTokens = 16;
 
 struct DecodeParams {
   void* out;
   const void* q;
+  int64_t q_stride;  // elements between sequences
+  const void* k;
+  int64_t k_stride;
+  const void* v;
+  int64_t v_stride;
+  const int32_t* positions;
+  const int32_t* slot_mapping;
+  const float* inv_freq;  // fused mode: RoPE table; else nullptr
+  void* pool;
   const int32_t* block_tables;
   const int32_t* seq_lens;
   int max_blocks;
@@ -54,20 +94,47 @@ struct DecodeParams {
   int num_blocks;
   int num_hg;  // head groups = n_kv / HPC
   int n_cta;
-  float scale_log2;  // scale * log2(e)
-  int early_prologue;  // 1: seq_lens/block tables may be read before the PDL wait
-  int* meta;         // [0] = pages per CTA, [1] = total pages, [2..] = page prefix sums
-  float* part_ml;    // [n_cta][2][HPC * GP][2]   (running max in log2 units, sum)
-  float* part_o;     // [n_cta][2][HPC * GP][D]   (unnormalised output)
+  float scale_log2;    // scale * log2(e)
+  int fused;           // 1: RoPE + K/V write inside the kernel
+  int early_prologue;  // 1: seq_lens may be read before the PDL wait
+  int* counters;       // [n_kv * num_seqs], zero between calls
+  float* part_ml;      // [n_cta * 2 * HPC][NT][4 lanes][4]
+  float* part_o;       // [n_cta * 2 * HPC][NT * D/16][32 lanes][4]
   int* err;
 };
+
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
+// Release this piece (fence, then a relaxed increment): returns the counter
+// value before the increment.
+__device__ __forceinline__ int arrive_piece(int* counter) {
+  fence_acq_rel_gpu();
+  int old;
+  asm volatile("atom.relaxed.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-template <int D, int HPC, typename T>
+template <int D, int HPC>
 struct DecodeShape {
   static constexpr int kDHalves = D / 64;
   static constexpr int kRowBytes = 128;  // 64 elements of 16 bits
@@ -77,8 +144,8 @@ struct DecodeShape {
 };
 
 __device__ __forceinline__ int upper_bound_pref(const int* pref, int n, int f) {
-  // Largest s in [0, n) with pref[s] <= f (pref is non-decreasing, pref[0] = 0).
-  int lo = 0, hi = n;  // invariant: pref[lo] <= f, answer in [lo, hi)
+  // Largest s in [0, n) with pref[s] <= f (pref non-decreasing, pref[0] = 0).
+  int lo = 0, hi = n;
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (pref[mid] <= f) lo = mid; else hi = mid;
@@ -86,16 +153,94 @@ __device__ __forceinline__ int upper_bound_pref(const int* pref, int n, int f) {
   return lo;
 }
 
+// RoPE of one element pair with the reference's rounding points
+// (layers/rotary_embedding.py:20-24): x*cos, rotate_half(x)*sin and their sum
+// each rounded to T.  `lo` is element j, `hi` element j + D/2.
+template <typename T>
+__device__ __forceinline__ void rope_pair(float lo, float hi, float cs, float sn, float& out_lo,
+                                          float& out_hi) {
+  const float a_lo = Elt<T>::to_f(Elt<T>::from_f(lo * cs));
+  const float b_lo = Elt<T>::to_f(Elt<T>::from_f(-hi * sn));
+  const float a_hi = Elt<T>::to_f(Elt<T>::from_f(hi * cs));
+  const float b_hi = Elt<T>::to_f(Elt<T>::from_f(lo * sn));
+  out_lo = Elt<T>::to_f(Elt<T>::from_f(a_lo + b_lo));
+  out_hi = Elt<T>::to_f(Elt<T>::from_f(a_hi + b_hi));
+}
+
+// Normalises the O^T fragments by l and stores the G query heads of kv head
+// kvh of sequence s (fragment: d = mt*16 + g (+8), heads 2c, 2c+1 of n-tile nt).
+template <typename T, int D, int NT>
+__device__ __forceinline__ void store_output(T* obase, int s, int kvh, int n_q, int G, int g,
+                                             int c, const float (&l)[NT][2],
+                                             const float (&o)[NT][D / 16][4]) {
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const float inv0 = 1.f / l[nt][0], inv1 = 1.f / l[nt][1];
+    const int n0 = nt * 8 + 2 * c;
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt) {
+      const int d = mt * 16 + g;
+      if (n0 < G) {
+        T* row = obase + (static_cast<size_t>(s) * n_q + kvh * G + n0) * D;
+        row[d] = Elt<T>::from_f(o[nt][mt][0] * inv0);
+        row[d + 8] = Elt<T>::from_f(o[nt][mt][2] * inv0);
+      }
+      if (n0 + 1 < G) {
+        T* row = obase + (static_cast<size_t>(s) * n_q + kvh * G + n0 + 1) * D;
+        row[d] = Elt<T>::from_f(o[nt][mt][1] * inv1);
+        row[d + 8] = Elt<T>::from_f(o[nt][mt][3] * inv1);
+      }
+    }
+  }
+}
+
+// cos/sin of sequence s's position at frequency jj, rounded to T
+// (rotary_embedding.py:47-53, 71-72): the fp32 angle pos * inv_freq[jj]
+// (one product, as torch.outer computes it), evaluated in double precision.
+template <typename T, typename Params>
+__device__ __forceinline__ void rope_entry(const Params& p, int s, int jj, float* cs, float* sn) {
+  const int pos = p.positions[s];
+  if (pos < 0) set_error(p.err, kDevErrPositionRange);
+  const float ang = static_cast<float>(pos) * p.inv_freq[jj];
+  double sd, cd;
+  sincos(static_cast<double>(ang), &sd, &cd);
+  cs[jj] = Elt<T>::to_f(Elt<T>::from_f(static_cast<float>(cd)));
+  sn[jj] = Elt<T>::to_f(Elt<T>::from_f(static_cast<float>(sd)));
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack2(uint32_t w, float& a, float& b) {
+  const T* e = reinterpret_cast<const T*>(&w);
+  a = Elt<T>::to_f(e[0]);
+  b = Elt<T>::to_f(e[1]);
+}
+
 template <typename T, int D, int HPC, int NT>
-__global__ void __launch_bounds__(DecodeShape<D, HPC, T>::kThreads, kCtasPerSm)
+__global__ void __launch_bounds__(DecodeShape<D, HPC>::kThreads, kCtasPerSm)
 paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
-  using Shape = DecodeShape<D, HPC, T>;
-  constexpr int GP = 8 * NT;
+  using Shape = DecodeShape<D, HPC>;
   constexpr int KS = D / 16;  // k-steps over head_dim, and m-tiles of O^T
+  constexpr int HALF = D / 2;
 
   __shared__ uint64_t full_bar[kStages];
   __shared__ uint64_t empty_bar[kStages];
+  __shared__ int stage_blk[kStages];
   __shared__ volatile int s_abort;
+  __shared__ float rope_cs[HPC][HALF];  // per-warp table beyond kSegTables segments
+  __shared__ float rope_sn[HPC][HALF];
+  __shared__ float seg_cs[kSegTables][HALF];  // tables of this CTA's first segments
+  __shared__ float seg_sn[kSegTables][HALF];
+  __shared__ int seg_seq[kSegTables];
+  __shared__ int seg_hg[kSegTables];
+  __shared__ int seg_ctx[kSegTables];
+  __shared__ int seg_slot[kSegTables];
+  __shared__ int n_seg_tables;
+  // Per-segment inputs staged with cp.async right after the PDL wait, so a
+  // segment switch never waits on a global load behind the page stream:
+  // the query rows of each kv head, and (fused) the new token's K and V rows.
+  __shared__ __align__(16) T seg_q[kSegTables][HPC][8 * NT][D];
+  __shared__ __align__(16) T seg_kv[kSegTables][HPC][2][D];
+  __shared__ uint64_t loop_done_bar;  // all consumer warps finished with the ring
   extern __shared__ uint8_t dyn_smem[];
 
   const int tid = threadIdx.x;
@@ -103,7 +248,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
   const int lane = tid & 31;
   const int num_seqs = p.num_seqs;
 
-  // Dynamic shared memory: [stage ring, 1024-aligned][prefix sums of pages].
+  // Dynamic shared memory: [stage ring, 1024-aligned][page prefix sums].
   const uint32_t dyn_base = smem_u32(dyn_smem);
   const uint32_t ring_off = ((dyn_base + 1023u) & ~1023u) - dyn_base;
   uint8_t* ring = dyn_smem + ring_off;
@@ -111,16 +256,16 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
 
   if (tid == 0) {
     s_abort = 0;
+    n_seg_tables = 0;
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&full_bar[i], 1);
       mbar_init(&empty_bar[i], HPC);
     }
+    mbar_init(&loop_done_bar, HPC);
     fence_mbar_init();
   }
-  // With programmatic dependent launch this CTA may start before the kernel
-  // ahead of it in the stream has finished.  seq_lens and block tables are
-  // only read early when the caller knows that kernel does not write them
-  // (the decode-step entry point, whose predecessor is kernel 1).
+  // seq_lens are read before the PDL wait only when the caller knows the
+  // kernel ahead of this one does not write them.
   if (!p.early_prologue) pdl_wait();
 
   // ── per-sequence page counts and their prefix sums ─────────────────────────
@@ -158,40 +303,113 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
   const long long u_begin = static_cast<long long>(blockIdx.x) * chunk;
   const long long u_end = u_begin + chunk < U ? u_begin + chunk : U;
 
-  // q and the pool may still be being written by the kernel before this one.
-  if (p.early_prologue) pdl_wait();
-  if (blockIdx.x == 0) {
-    // Work split for the combine kernel, and zero rows for empty sequences.
-    for (int i = tid; i <= num_seqs; i += blockDim.x) p.meta[2 + i] = pref[i];
-    if (tid == 0) {
-      p.meta[0] = static_cast<int>(chunk);
-      p.meta[1] = TP;
+  // Work decode for a unit: its head group and physical block (producer) or
+  // its sequence (consumers).
+  // (The block id is range-checked where it is used, so the load is not
+  // waited for here.)
+  auto unit_block = [&](long long u, int& hg, int& phys) {
+    hg = static_cast<int>(u / TP);
+    const int f = static_cast<int>(u - static_cast<long long>(hg) * TP);
+    const int s = upper_bound_pref(pref, num_seqs, f);
+    phys = p.block_tables[static_cast<size_t>(s) * p.max_blocks + (f - pref[s])];
+  };
+  // Early work that only needs host-written inputs (block tables, positions):
+  // the producer's first 32 table entries and, in fused mode, the RoPE tables
+  // of this CTA's first segments (one per sequence, shared by all heads).
+  int pre_phys = 0, pre_hg = 0;
+  if (tid == 0) {
+    // This CTA's first segments (one sequence each): length, new-token slot.
+    long long uu = u_begin;
+    int k = 0;
+    for (; k < kSegTables && uu < u_end; ++k) {
+      const int hg = static_cast<int>(uu / TP);
+      const int f = static_cast<int>(uu - static_cast<long long>(hg) * TP);
+      const int sq = upper_bound_pref(pref, num_seqs, f);
+      seg_seq[k] = sq;
+      seg_hg[k] = hg;
+      seg_ctx[k] = p.seq_lens[sq];
+      seg_slot[k] = p.fused ? p.slot_mapping[sq] : -1;
+      uu += pref[sq + 1] - f;
     }
-    for (int s = 0; s < num_seqs; ++s) {
+    n_seg_tables = k;
+  }
+  if (p.early_prologue && u_begin < u_end && warp == 0 && u_begin + lane < u_end) {
+    unit_block(u_begin + lane, pre_hg, pre_phys);
+  }
+  __syncthreads();
+  if (p.fused) {
+    // RoPE tables of those segments (positions are host-written inputs).
+    for (int e = tid; e < n_seg_tables * HALF; e += blockDim.x) {
+      const int k = e / HALF, jj = e - k * HALF;
+      rope_entry<T>(p, seg_seq[k], jj, seg_cs[k], seg_sn[k]);
+    }
+    __syncthreads();
+  }
+
+  // q/k/v and the pool may still be being written by the previous kernel.
+  if (p.early_prologue) pdl_wait();
+  pdl_trigger();
+  if (blockIdx.x == 0) {
+    // Zero rows for empty sequences (they own no work unit, so in fused mode
+    // their new K/V is not written either: flagged).  One thread per sequence.
+    for (int s = tid; s < num_seqs; s += blockDim.x) {
       if (pref[s + 1] == pref[s]) {
+        if (p.fused && p.slot_mapping[s] >= 0) set_error(p.err, kDevErrSlotNotLast);
         T* o = static_cast<T*>(p.out) + static_cast<size_t>(s) * p.n_q * D;
-        for (int e = tid; e < p.n_q * D; e += blockDim.x) o[e] = Elt<T>::from_f(0.f);
+        for (int e = 0; e < p.n_q * D; ++e) o[e] = Elt<T>::from_f(0.f);
       }
     }
   }
-  pdl_trigger();
   if (u_begin >= u_end) return;
+
+  if (warp > 0) {
+    // Stage this warp's kv-head rows of the first segments: the G query rows
+    // and, in fused mode, the new token's K and V.
+    const int h = warp - 1;
+    for (int k = 0; k < n_seg_tables; ++k) {
+      const int sq = seg_seq[k];
+      const int kvh = seg_hg[k] * HPC + h;
+      const T* qsrc = static_cast<const T*>(p.q) + static_cast<size_t>(sq) * p.q_stride +
+                      static_cast<size_t>(kvh) * p.G * D;
+      T* qdst = &seg_q[k][h][0][0];
+      for (int ci = lane; ci < p.G * (D / 8); ci += 32) cp_async16(qdst + ci * 8, qsrc + ci * 8);
+      if (p.fused) {
+        const T* ksrc = static_cast<const T*>(p.k) + static_cast<size_t>(sq) * p.k_stride +
+                        static_cast<size_t>(kvh) * D;
+        const T* vsrc = static_cast<const T*>(p.v) + static_cast<size_t>(sq) * p.v_stride +
+                        static_cast<size_t>(kvh) * D;
+        for (int ci = lane; ci < 2 * (D / 8); ci += 32) {
+          const bool is_v = ci >= D / 8;
+          const int cc = is_v ? ci - D / 8 : ci;
+          cp_async16(&seg_kv[k][h][is_v ? 1 : 0][cc * 8], (is_v ? vsrc : ksrc) + cc * 8);
+        }
+      }
+    }
+    cp_async_commit();
+  }
 
   if (warp == 0) {
     // ── producer: one TMA per 64 columns per page ────────────────────────────
     if (lane == 0) prefetch_tmap(&tmap);
     int it = 0;
+    // Block-table entries are fetched one batch of 32 ahead, so their load
+    // latency (long while the page stream keeps HBM queues full) is hidden.
+    int cur_phys = 0, cur_hg = 0;
+    if (p.early_prologue) {
+      cur_phys = pre_phys;
+      cur_hg = pre_hg;
+    } else if (u_begin + lane < u_end) {
+      unit_block(u_begin + lane, cur_hg, cur_phys);
+    }
     for (long long base = u_begin; base < u_end; base += 32) {
-      const long long u = base + lane;
-      int phys = 0, hg = 0;
-      if (u < u_end) {
-        hg = static_cast<int>(u / TP);
-        const int f = static_cast<int>(u - static_cast<long long>(hg) * TP);
-        const int s = upper_bound_pref(pref, num_seqs, f);
-        const int j = f - pref[s];
-        phys = p.block_tables[static_cast<size_t>(s) * p.max_blocks + j];
-        if (phys < 0 || phys >= p.num_blocks) set_error(p.err, kDevErrBlockRange);
+      int nxt_phys = 0, nxt_hg = 0;
+      if (base + 32 + lane < u_end) unit_block(base + 32 + lane, nxt_hg, nxt_phys);
+      const int phys = cur_phys, hg = cur_hg;
+      if (base + lane < u_end && (phys < 0 || phys >= p.num_blocks)) {
+        set_error(p.err, kDevErrBlockRange);
       }
+      cur_phys = nxt_phys;
+      cur_hg = nxt_hg;
       const int n = static_cast<int>(u_end - base < 32 ? u_end - base : 32);
       for (int k = 0; k < n; ++k, ++it) {
         const int ph = __shfl_sync(0xffffffffu, phys, k);
@@ -202,6 +420,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
           if (!mbar_wait(&empty_bar[stage], (round & 1u) ^ 1u, p.err)) {
             s_abort = 1;
           } else {
+            stage_blk[stage] = ph;
             mbar_arrive_expect_tx(&full_bar[stage], Shape::kStageBytes);
             uint8_t* dst = ring + stage * Shape::kStageBytes;
 #pragma unroll
@@ -223,7 +442,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
   const int g = lane >> 2;  // MMA row group
   const int c = lane & 3;   // MMA column pair
   const int mi = lane >> 3, r = lane & 7;
-  // Per-lane byte offsets inside one [64-column] tile for ldmatrix.
   uint32_t k_off[4], v_off[4];
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks) {
@@ -237,7 +455,29 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
   const uint32_t ring_u32 = smem_u32(ring);
   const T* qbase = static_cast<const T*>(p.q);
   T* obase = static_cast<T*>(p.out);
+  int kseg = 0;
 
+  {
+    // Pull the Q rows of this CTA's first few segments into L2 now, so the
+    // loads at later segment switches do not queue behind the page stream.
+    long long uu = u_begin;
+    for (int k = 0; k < 4 && uu < u_end; ++k) {
+      const int hg = static_cast<int>(uu / TP);
+      const int f = static_cast<int>(uu - static_cast<long long>(hg) * TP);
+      const int s = upper_bound_pref(pref, num_seqs, f);
+      const char* qrow = reinterpret_cast<const char*>(
+          qbase + static_cast<size_t>(s) * p.q_stride + static_cast<size_t>((hg * HPC + h) * p.G) * D);
+      const int bytes = p.G * D * static_cast<int>(sizeof(T));
+      for (int off = lane * 128; off < bytes; off += 32 * 128) {
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(qrow + off));
+      }
+      uu += pref[s + 1] - pref[s] - (f - pref[s]);
+    }
+  }
+  int pend_s[2], pend_kvh[2], pend_c0[2], pend_c1[2];
+  int pend_old[2] = {-1, -1};  // counter value before our arrival (lane 0)
+  int n_pend = 0, n_arrived = 0;
+  int arrive_at = -1;  // page count after which the oldest piece arrives
   int it = 0;
   long long u = u_begin;
   while (u < u_end) {
@@ -249,7 +489,35 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
     const long long left = u_end - u;
     const int j1 = (seg_pages - j0) < left ? seg_pages : j0 + static_cast<int>(left);
     const int kvh = hg * HPC + h;
-    const int ctx = p.seq_lens[s];
+    const bool staged = kseg < n_seg_tables;
+    if (kseg == 0) {
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      __syncwarp();
+    }
+    const int ctx = staged ? seg_ctx[kseg] : p.seq_lens[s];
+    const T* q_rows = staged ? &seg_q[kseg][h][0][0]
+                             : qbase + static_cast<size_t>(s) * p.q_stride +
+                                   static_cast<size_t>(kvh) * p.G * D;
+    const T* new_k = staged ? &seg_kv[kseg][h][0][0]
+                            : static_cast<const T*>(p.k) + static_cast<size_t>(s) * p.k_stride +
+                                  static_cast<size_t>(kvh) * D;
+    const T* new_v = staged ? &seg_kv[kseg][h][1][0]
+                            : static_cast<const T*>(p.v) + static_cast<size_t>(s) * p.v_stride +
+                                  static_cast<size_t>(kvh) * D;
+    const int new_slot = staged ? seg_slot[kseg] : (p.fused ? p.slot_mapping[s] : -1);
+
+    const float* cs_tab = rope_cs[h];
+    const float* sn_tab = rope_sn[h];
+    if (p.fused) {
+      if (staged) {
+        cs_tab = seg_cs[kseg];
+        sn_tab = seg_sn[kseg];
+      } else {
+        for (int jj = lane; jj < HALF; jj += 32) rope_entry<T>(p, s, jj, rope_cs[h], rope_sn[h]);
+        __syncwarp();
+      }
+    }
+    ++kseg;
 
     // Q^T as the B operand: b0 = Q[n][ks*16 + 2c..], b1 = Q[n][ks*16 + 8 + 2c..].
     uint32_t qf[NT][KS][2];
@@ -257,11 +525,29 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
     for (int nt = 0; nt < NT; ++nt) {
       const int n = nt * 8 + g;
       const bool valid = n < p.G;
-      const T* qrow = qbase + (static_cast<size_t>(s) * p.n_q + kvh * p.G + (valid ? n : 0)) * D;
+      const T* qrow = q_rows + static_cast<size_t>(valid ? n : 0) * D;
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
         qf[nt][ks][0] = valid ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * c) : 0u;
         qf[nt][ks][1] = valid ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * c) : 0u;
+      }
+      if (p.fused) {
+        // Rotate in registers: element d pairs with d + D/2, which this lane
+        // holds in k-step ks + KS/2 at the same offsets.
+#pragma unroll
+        for (int ks = 0; ks < KS / 2; ++ks) {
+#pragma unroll
+          for (int w = 0; w < 2; ++w) {
+            const int j = ks * 16 + w * 8 + 2 * c;
+            float l0, l1, h0, h1, o0, o1, p0, p1;
+            unpack2<T>(qf[nt][ks][w], l0, l1);
+            unpack2<T>(qf[nt][ks + KS / 2][w], h0, h1);
+            rope_pair<T>(l0, h0, cs_tab[j], sn_tab[j], o0, p0);
+            rope_pair<T>(l1, h1, cs_tab[j + 1], sn_tab[j + 1], o1, p1);
+            qf[nt][ks][w] = Elt<T>::pack(o0, o1);
+            qf[nt][ks + KS / 2][w] = Elt<T>::pack(p0, p1);
+          }
+        }
       }
     }
     float m_run[NT][2], l_run[NT][2], o[NT][KS][4];
@@ -280,6 +566,65 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
         break;
       }
       const uint32_t sbase = ring_u32 + stage * Shape::kStageBytes;
+
+      if (p.fused && j == seg_pages - 1) {
+        // This warp owns the new token of (s, kvh): rotate K, write K and V to
+        // the pool slot and into this page's shared-memory copy.
+        const int slot = new_slot;
+        const int tok = slot & (kPageTokens - 1);
+        const int blk = slot >> 4;
+        const bool in_pool = slot >= 0 && blk < p.num_blocks;
+        if (!in_pool && lane == 0 && slot >= 0) set_error(p.err, kDevErrSlotRange);
+        const bool here = in_pool && blk == stage_blk[stage];
+        // The new token must sit in the sequence's last page, which only this
+        // CTA reads in this launch; anywhere else the write could race a read.
+        if (in_pool && !here && lane == 0) set_error(p.err, kDevErrSlotNotLast);
+        constexpr int kChunks = D / 8;  // 16-byte chunks per row
+        if (lane < 2 * kChunks && in_pool) {
+          const bool is_v = lane >= kChunks;
+          const int ci = is_v ? lane - kChunks : lane;
+          uint4 val;
+          if (is_v) {
+            val = *reinterpret_cast<const uint4*>(new_v + ci * 8);
+          } else {
+            const T* krow = new_k;
+            const int base_e = ci * 8;
+            const int partner = base_e < HALF ? base_e + HALF : base_e - HALF;
+            const uint4 mine = *reinterpret_cast<const uint4*>(krow + base_e);
+            const uint4 other = *reinterpret_cast<const uint4*>(krow + partner);
+            const T* me = reinterpret_cast<const T*>(&mine);
+            const T* ot = reinterpret_cast<const T*>(&other);
+            T res[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int jj = (base_e + e) & (HALF - 1);
+              float lo, hi, out_lo, out_hi;
+              if (base_e < HALF) {
+                lo = Elt<T>::to_f(me[e]);
+                hi = Elt<T>::to_f(ot[e]);
+              } else {
+                lo = Elt<T>::to_f(ot[e]);
+                hi = Elt<T>::to_f(me[e]);
+              }
+              rope_pair<T>(lo, hi, cs_tab[jj], sn_tab[jj], out_lo, out_hi);
+              res[e] = Elt<T>::from_f(base_e < HALF ? out_lo : out_hi);
+            }
+            val = *reinterpret_cast<const uint4*>(res);
+          }
+          T* dst = static_cast<T*>(p.pool) +
+                   ((static_cast<size_t>(blk) * 2 + (is_v ? 1 : 0)) * kPageTokens + tok) *
+                       static_cast<size_t>(p.n_kv) * D +
+                   static_cast<size_t>(kvh) * D + ci * 8;
+          *reinterpret_cast<uint4*>(dst) = val;
+          if (here) {
+            const int dh = ci >> 3, cc = ci & 7;
+            uint8_t* row = ring + stage * Shape::kStageBytes + dh * Shape::kTileBytes +
+                           (((is_v ? 1 : 0) * HPC + h) * kPageTokens + tok) * Shape::kRowBytes;
+            *reinterpret_cast<uint4*>(row + ((cc ^ (tok & 7)) << 4)) = val;
+          }
+        }
+        __syncwarp();
+      }
 
       // S^T = K . Q^T
       float sc[NT][4];
@@ -339,10 +684,19 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[stage]);
+      if (n_arrived < n_pend && it >= arrive_at) {
+        // Arrive for a piece published a couple of pages ago: its stores are
+        // done by now, so the release fence is cheap, and the counter's
+        // answer is only needed after the last page.
+        if (lane == 0) {
+          pend_old[n_arrived] = arrive_piece(&p.counters[static_cast<size_t>(pend_kvh[n_arrived]) * num_seqs + pend_s[n_arrived]]);
+        }
+        ++n_arrived;
+      }
     }
     if (s_abort) break;
 
-    // Sum each head's l over the 8 row groups.
+    // Sum each head's l over the 8 row groups (m is already uniform).
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -354,116 +708,128 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
 
     if (j0 == 0 && j1 == seg_pages) {
       // The whole sequence was in this CTA: normalise and store.
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const float inv0 = 1.f / l_run[nt][0], inv1 = 1.f / l_run[nt][1];
-        const int n0 = nt * 8 + 2 * c;
-#pragma unroll
-        for (int mt = 0; mt < KS; ++mt) {
-          const int d = mt * 16 + g;
-          if (n0 < p.G) {
-            T* row = obase + (static_cast<size_t>(s) * p.n_q + kvh * p.G + n0) * D;
-            row[d] = Elt<T>::from_f(o[nt][mt][0] * inv0);
-            row[d + 8] = Elt<T>::from_f(o[nt][mt][2] * inv0);
-          }
-          if (n0 + 1 < p.G) {
-            T* row = obase + (static_cast<size_t>(s) * p.n_q + kvh * p.G + n0 + 1) * D;
-            row[d] = Elt<T>::from_f(o[nt][mt][1] * inv1);
-            row[d + 8] = Elt<T>::from_f(o[nt][mt][3] * inv1);
-          }
-        }
-      }
+      store_output<T, D, NT>(obase, s, kvh, p.n_q, p.G, g, c, l_run, o);
     } else {
-      // Split sequence: publish this piece for the combine kernel.
+      // Split sequence: publish this piece now; the arrival (and the merge,
+      // for the last piece) waits until this CTA's pages are all streamed,
+      // so a round trip to the counter never stalls the page pipeline.
       const long long seg_first = static_cast<long long>(hg) * TP + pref[s];
       const int c0 = static_cast<int>(seg_first / chunk);
+      const int c1 = static_cast<int>((seg_first + seg_pages - 1) / chunk);
       const int slot = (static_cast<int>(blockIdx.x) == c0) ? 1 : 0;
-      const size_t rec = (static_cast<size_t>(blockIdx.x) * 2 + slot) * HPC * GP +
-                         static_cast<size_t>(h) * GP;
-      float* ml = p.part_ml + rec * 2;
-      float* po = p.part_o + rec * D;
+      const size_t rec = (static_cast<size_t>(blockIdx.x) * 2 + slot) * HPC + h;
+      float4* po = reinterpret_cast<float4*>(p.part_o) + rec * NT * KS * 32;
+      float4* pml = reinterpret_cast<float4*>(p.part_ml) + rec * NT * 4;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const int n0 = nt * 8 + 2 * c;
-        if (g == 0) {
-          *reinterpret_cast<float4*>(ml + n0 * 2) =
-              make_float4(m_run[nt][0], l_run[nt][0], m_run[nt][1], l_run[nt][1]);
-        }
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
-          const int d = mt * 16 + g;
-          po[n0 * D + d] = o[nt][mt][0];
-          po[(n0 + 1) * D + d] = o[nt][mt][1];
-          po[n0 * D + d + 8] = o[nt][mt][2];
-          po[(n0 + 1) * D + d + 8] = o[nt][mt][3];
+          __stcg(po + (nt * KS + mt) * 32 + lane,
+                 make_float4(o[nt][mt][0], o[nt][mt][1], o[nt][mt][2], o[nt][mt][3]));
+        }
+        if (g == 0) {
+          __stcg(pml + nt * 4 + c,
+                 make_float4(m_run[nt][0], l_run[nt][0], m_run[nt][1], l_run[nt][1]));
         }
       }
+      // Only a CTA's first and last segments can be split: at most two.
+      if (n_pend == 2) {
+        set_error(p.err, kDevErrSeqLen);
+        break;
+      }
+      pend_s[n_pend] = s;
+      pend_kvh[n_pend] = kvh;
+      pend_c0[n_pend] = c0;
+      pend_c1[n_pend] = c1;
+      ++n_pend;
+      arrive_at = it + 2;
     }
     u += (j1 - j0);
   }
-}
+  if (s_abort) return;
 
-// ── combine: merge the pieces of sequences that were split between CTAs ──────
-//
-// Grid (num_hg * num_seqs, ceil(HPC*G*D / 256)); one thread per output element.
-// Unsplit sequences were written directly by the main kernel and are skipped.
-template <typename T>
-__global__ void __launch_bounds__(256)
-paged_decode_combine_kernel(const DecodeParams p, int hpc, int gp, int D) {
-  pdl_wait();  // partials and meta come from the kernel launched just before
-  const int seg = blockIdx.x;
-  const int s = seg % p.num_seqs;
-  const int hg = seg / p.num_seqs;
-  const int chunk = p.meta[0];
-  const int TP = p.meta[1];
-  const int pref_s = p.meta[2 + s];
-  const int seg_pages = p.meta[3 + s] - pref_s;
-  if (seg_pages <= 0) return;
-  const long long first = static_cast<long long>(hg) * TP + pref_s;
-  const int c0 = static_cast<int>(first / chunk);
-  const int c1 = static_cast<int>((first + seg_pages - 1) / chunk);
-  if (c0 == c1) return;
-  const int e = blockIdx.y * blockDim.x + threadIdx.x;
-  const int G = p.G;
-  if (e >= hpc * G * D) return;
-  const int h = e / (G * D);
-  const int n = (e / D) % G;
-  const int d = e % D;
-  float M = -INFINITY, num = 0.f, den = 0.f;
-  for (int cc = c0; cc <= c1; cc += 4) {
-    float m4[4], l4[4], o4[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int c = cc + k;
-      if (c <= c1) {
-        const size_t rec = (static_cast<size_t>(c) * 2 + (c == c0 ? 1 : 0)) * hpc * gp +
-                           static_cast<size_t>(h) * gp + n;
-        const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml) + rec);
-        m4[k] = ml.x;
-        l4[k] = ml.y;
-        o4[k] = __ldcg(p.part_o + rec * D + d);
-      } else {
-        m4[k] = -INFINITY;
-        l4[k] = o4[k] = 0.f;
-      }
+  // Remaining arrivals (the last segment's piece, just published).
+  // __syncwarp orders every lane's partial stores before lane 0's release.
+  __syncwarp();
+  int last_mask = 0;
+  if (lane == 0) {
+    for (int i = n_arrived; i < n_pend; ++i) {
+      pend_old[i] = arrive_piece(&p.counters[static_cast<size_t>(pend_kvh[i]) * num_seqs + pend_s[i]]);
     }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      if (m4[k] == -INFINITY) continue;
-      if (m4[k] > M) {
-        const float r = fast_exp2(M - m4[k]);
-        num *= r;
-        den *= r;
-        M = m4[k];
-      }
-      const float w = fast_exp2(m4[k] - M);
-      num += w * o4[k];
-      den += w * l4[k];
+    for (int i = 0; i < n_pend; ++i) {
+      if (pend_old[i] == pend_c1[i] - pend_c0[i]) last_mask |= 1 << i;
     }
+    if (last_mask) fence_acq_rel_gpu();  // acquire the other pieces
   }
-  const int kvh = hg * hpc + h;
-  static_cast<T*>(p.out)[(static_cast<size_t>(s) * p.n_q + kvh * G + n) * D + d] =
-      Elt<T>::from_f(num / den);
+  last_mask = __shfl_sync(0xffffffffu, last_mask, 0);
+  __syncwarp();  // every lane's loads below come after lane 0's acquire
+  // The shared-memory ring is reused to stage the pieces to merge, once every
+  // consumer warp is done reading pages from it.
+  if (lane == 0) mbar_arrive(&loop_done_bar);
+  if (!last_mask) return;
+  if (!mbar_wait(&loop_done_bar, 0, p.err)) return;
+
+  // Stage every piece of every segment this warp merges into its slice of
+  // the ring with 16-byte cp.async (one round trip), then merge in registers.
+  constexpr int kPartO = NT * KS * 32;  // float4 per piece (fragment order)
+  constexpr int kPartML = NT * 4;
+  constexpr int kPartBytes = (kPartO + kPartML) * 16;
+  constexpr int kRegion = (kStages * Shape::kStageBytes / HPC) & ~15;
+  constexpr int kCap = kRegion / kPartBytes;
+  static_assert(kCap >= 2, "merge staging region too small");
+  float4* region = reinterpret_cast<float4*>(ring + h * kRegion);
+  for (int i = 0; i < n_pend; ++i) {
+    if (!(last_mask & (1 << i))) continue;
+    const int s = pend_s[i], kvh = pend_kvh[i], c0 = pend_c0[i], c1 = pend_c1[i];
+    float m_run[NT][2], l_run[NT][2], o[NT][KS][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      m_run[nt][0] = m_run[nt][1] = -INFINITY;
+      l_run[nt][0] = l_run[nt][1] = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
+    }
+    for (int b0 = c0; b0 <= c1; b0 += kCap) {
+      const int nb = (c1 - b0 + 1) < kCap ? (c1 - b0 + 1) : kCap;
+      for (int b = 0; b < nb; ++b) {
+        const int pc = b0 + b;
+        const size_t rr = (static_cast<size_t>(pc) * 2 + (pc == c0 ? 1 : 0)) * HPC + h;
+        const float4* qo = reinterpret_cast<const float4*>(p.part_o) + rr * kPartO;
+        const float4* qml = reinterpret_cast<const float4*>(p.part_ml) + rr * kPartML;
+        float4* so = region + b * (kPartO + kPartML);
+#pragma unroll
+        for (int v = 0; v < NT * KS; ++v) cp_async16(so + v * 32 + lane, qo + v * 32 + lane);
+        if (lane < kPartML) cp_async16(so + kPartO + lane, qml + lane);
+      }
+      cp_async_wait_all();
+      __syncwarp();
+      for (int b = 0; b < nb; ++b) {
+        const float4* so = region + b * (kPartO + kPartML);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const float4 m4 = so[kPartO + nt * 4 + c];
+          const float n0 = fmaxf(m_run[nt][0], m4.x), n1 = fmaxf(m_run[nt][1], m4.z);
+          const float a0 = fast_exp2(m_run[nt][0] - n0), a1 = fast_exp2(m_run[nt][1] - n1);
+          const float e0 = fast_exp2(m4.x - n0), e1 = fast_exp2(m4.z - n1);
+          m_run[nt][0] = n0;
+          m_run[nt][1] = n1;
+          l_run[nt][0] = l_run[nt][0] * a0 + m4.y * e0;
+          l_run[nt][1] = l_run[nt][1] * a1 + m4.w * e1;
+#pragma unroll
+          for (int mt = 0; mt < KS; ++mt) {
+            const float4 v4 = so[(nt * KS + mt) * 32 + lane];
+            o[nt][mt][0] = o[nt][mt][0] * a0 + v4.x * e0;
+            o[nt][mt][1] = o[nt][mt][1] * a1 + v4.y * e1;
+            o[nt][mt][2] = o[nt][mt][2] * a0 + v4.z * e0;
+            o[nt][mt][3] = o[nt][mt][3] * a1 + v4.w * e1;
+          }
+        }
+      }
+      __syncwarp();  // the slots are reused by the next batch
+    }
+    if (lane == 0) p.counters[static_cast<size_t>(kvh) * num_seqs + s] = 0;
+    store_output<T, D, NT>(obase, s, kvh, p.n_q, p.G, g, c, l_run, o);
+  }
 }
 
 // ── host side ────────────────────────────────────────────────────────────────
@@ -475,7 +841,7 @@ struct DecodeConfig {
 
 static bool pick_config(int n_q, int n_kv, int D, DecodeConfig* cfg) {
   if (D != 64 && D != 128) return false;
-  if (n_kv <= 0 || n_q <= 0 || n_q % n_kv) return false;
+  if (n_kv <= 0 || n_kv > kMaxKvHeads || n_q <= 0 || n_q % n_kv) return false;
   const int G = n_q / n_kv;
   if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16) return false;
   const int want = 256 / D;  // heads per CTA for a 16 KiB page tile
@@ -490,24 +856,26 @@ static bool pick_config(int n_q, int n_kv, int D, DecodeConfig* cfg) {
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Workspace layout: [meta: (num_seqs + 3) ints][part_ml][part_o], each 256-aligned.
+// Workspace layout: [counters][part_ml][part_o], each 256-byte aligned.  The
+// counter region has a fixed size (kMaxSeqs * kMaxKvHeads ints) whatever the
+// call's shape, so a workspace reused for another shape still finds zeros
+// there: it must be zero before the first call, and every call leaves the
+// counters it used at zero.
 struct WorkspaceLayout {
-  size_t meta, ml, o, total;
+  size_t counters, ml, o, total;
 };
 
-static WorkspaceLayout workspace_layout(int num_seqs, int D, const DecodeConfig& cfg, int n_cta) {
+static WorkspaceLayout workspace_layout(int num_seqs, int n_kv, int D, const DecodeConfig& cfg,
+                                        int n_cta) {
   WorkspaceLayout w;
-  const size_t recs = static_cast<size_t>(n_cta) * 2 * cfg.hpc * 8 * cfg.nt;
-  w.meta = 0;
-  w.ml = align256(static_cast<size_t>(num_seqs + 3) * sizeof(int));
-  w.o = w.ml + align256(recs * 2 * sizeof(float));
-  w.total = w.o + align256(recs * D * sizeof(float));
-  return w;
-}
-
-static size_t workspace_bytes(int num_seqs, int n_kv, int D, const DecodeConfig& cfg, int n_cta) {
+  const size_t recs = static_cast<size_t>(n_cta) * 2 * cfg.hpc;
+  (void)num_seqs;
   (void)n_kv;
-  return workspace_layout(num_seqs, D, cfg, n_cta).total;
+  w.counters = 0;
+  w.ml = align256(static_cast<size_t>(kMaxKvHeads) * kMaxSeqs * sizeof(int));
+  w.o = w.ml + align256(recs * cfg.nt * 4 * 4 * sizeof(float));
+  w.total = w.o + align256(recs * cfg.nt * (D / 16) * 32 * 4 * sizeof(float));
+  return w;
 }
 
 // Launches `kernel` with programmatic dependent launch enabled, so it may
@@ -531,7 +899,7 @@ static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 
 template <typename T, int D, int HPC, int NT>
 static int launch_decode(const CUtensorMap& tmap, const DecodeParams& p, cudaStream_t s) {
-  using Shape = DecodeShape<D, HPC, T>;
+  using Shape = DecodeShape<D, HPC>;
   const size_t smem = 1024 + kStages * Shape::kStageBytes + (p.num_seqs + 1) * sizeof(int);
   static std::once_flag flags[64];
   int dev = 0;
@@ -542,18 +910,10 @@ static int launch_decode(const CUtensorMap& tmap, const DecodeParams& p, cudaStr
                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                          1024 + kStages * Shape::kStageBytes + (kMaxSeqs + 1) * sizeof(int));
   });
-  cudaError_t e = launch_pdl(paged_decode_kernel<T, D, HPC, NT>, dim3(p.n_cta),
-                             dim3(Shape::kThreads), smem, s, tmap, p);
+  const cudaError_t e = launch_pdl(paged_decode_kernel<T, D, HPC, NT>, dim3(p.n_cta),
+                                   dim3(Shape::kThreads), smem, s, tmap, p);
   if (e != cudaSuccess) {
     return fail(VMPS_ERR_CUDA, "paged_decode_attention: launch failed: %s", cudaGetErrorString(e));
-  }
-  const int elems = HPC * p.G * D;
-  e = launch_pdl(paged_decode_combine_kernel<T>,
-                 dim3(p.num_hg * p.num_seqs, (elems + 255) / 256), dim3(256), 0, s, p, HPC,
-                 8 * NT, D);
-  if (e != cudaSuccess) {
-    return fail(VMPS_ERR_CUDA, "paged_decode_attention: combine launch failed: %s",
-                cudaGetErrorString(e));
   }
   return VMPS_OK;
 }
@@ -578,84 +938,67 @@ static int dispatch_decode(const DecodeConfig& cfg, int D, const CUtensorMap& tm
               cfg.hpc, cfg.nt);
 }
 
-}  // namespace vmps
-
-extern "C" size_t vmps_paged_decode_workspace_bytes(int num_seqs, int n_q, int n_kv, int head_dim,
-                                                    int dtype) {
-  using namespace vmps;
-  DecodeConfig cfg;
-  if (num_seqs < 0 || (dtype != VMPS_DTYPE_F16 && dtype != VMPS_DTYPE_BF16) ||
-      !pick_config(n_q, n_kv, head_dim, &cfg)) {
-    return 0;
-  }
-  int sms = 0;
-  if (device_sm_count(&sms)) return 0;
-  return workspace_bytes(num_seqs > 0 ? num_seqs : 1, n_kv, head_dim, cfg, sms * kCtasPerSm);
-}
-
-extern "C" int vmps_paged_decode_workspace_init(void* workspace, size_t workspace_bytes,
-                                                void* stream) {
-  using namespace vmps;
-  clear_error();
-  if (!workspace && workspace_bytes) return fail(VMPS_ERR_INVALID_ARG, "workspace is NULL");
-  if (cudaMemsetAsync(workspace, 0, workspace_bytes, static_cast<cudaStream_t>(stream)) !=
-      cudaSuccess) {
-    return fail(VMPS_ERR_CUDA, "workspace memset failed: %s",
-                cudaGetErrorString(cudaGetLastError()));
-  }
-  return VMPS_OK;
-}
-
-namespace vmps {
-
-static int decode_enqueue(void* out, const void* q, const void* pool, const int32_t* block_tables,
+// Shared by both entry points.  `fused` adds RoPE + the K/V write.
+static int decode_enqueue(void* out, const void* q, int64_t q_stride, const void* k,
+                          int64_t k_stride, const void* v, int64_t v_stride,
+                          const int32_t* positions, const int32_t* slot_mapping,
+                          const float* inv_freq, void* pool, const int32_t* block_tables,
                           int max_blocks_per_seq, const int32_t* seq_lens, int num_seqs, int n_q,
                           int n_kv, int head_dim, int block_size, int num_blocks, float scale,
                           void* workspace, size_t workspace_bytes_given, int dtype, void* stream,
-                          int early_prologue) {
+                          int fused, const char* what) {
   if (num_seqs < 0 || num_blocks <= 0 || max_blocks_per_seq <= 0) {
-    return fail(VMPS_ERR_INVALID_ARG,
-                "paged_decode_attention: bad sizes (num_seqs=%d num_blocks=%d max_blocks=%d)",
-                num_seqs, num_blocks, max_blocks_per_seq);
+    return fail(VMPS_ERR_INVALID_ARG, "%s: bad sizes (num_seqs=%d num_blocks=%d max_blocks=%d)",
+                what, num_seqs, num_blocks, max_blocks_per_seq);
   }
   if (num_seqs == 0) return VMPS_OK;
   if (num_seqs > kMaxSeqs) {
-    return fail(VMPS_ERR_UNSUPPORTED, "paged_decode_attention: num_seqs %d > %d", num_seqs,
-                kMaxSeqs);
+    return fail(VMPS_ERR_UNSUPPORTED, "%s: num_seqs %d > %d", what, num_seqs, kMaxSeqs);
   }
   if (dtype != VMPS_DTYPE_F16 && dtype != VMPS_DTYPE_BF16) {
-    return fail(VMPS_ERR_INVALID_ARG, "paged_decode_attention: dtype %d", dtype);
+    return fail(VMPS_ERR_INVALID_ARG, "%s: dtype %d", what, dtype);
   }
   if (block_size != kPageTokens) {
-    return fail(VMPS_ERR_UNSUPPORTED, "paged_decode_attention: block_size %d (only 16 is built)",
-                block_size);
+    return fail(VMPS_ERR_UNSUPPORTED, "%s: block_size %d (only 16 is built)", what, block_size);
   }
   DecodeConfig cfg;
   if (!pick_config(n_q, n_kv, head_dim, &cfg)) {
     return fail(VMPS_ERR_UNSUPPORTED,
-                "paged_decode_attention: n_q=%d n_kv=%d head_dim=%d not supported "
-                "(head_dim 64/128, n_q/n_kv in 1,2,4,8,16)",
-                n_q, n_kv, head_dim);
+                "%s: n_q=%d n_kv=%d head_dim=%d not supported (head_dim 64/128, n_kv <= 64, "
+                "n_q/n_kv in 1,2,4,8,16)",
+                what, n_q, n_kv, head_dim);
   }
   if (!out || !q || !pool || !block_tables || !seq_lens) {
-    return fail(VMPS_ERR_INVALID_ARG, "paged_decode_attention: NULL pointer");
+    return fail(VMPS_ERR_INVALID_ARG, "%s: NULL pointer", what);
   }
-  if (!aligned16(pool) || (reinterpret_cast<uintptr_t>(q) & 3)) {
-    return fail(VMPS_ERR_ALIGNMENT, "paged_decode_attention: pool must be 16-byte aligned");
+  if (fused && (!k || !v || !positions || !slot_mapping || !inv_freq)) {
+    return fail(VMPS_ERR_INVALID_ARG, "%s: NULL k/v/positions/slot_mapping/inv_freq", what);
+  }
+  if (!aligned16(pool) || !aligned16(q) || (q_stride % 8) ||
+      (fused && (!aligned16(k) || !aligned16(v) || (k_stride % 8) || (v_stride % 8)))) {
+    return fail(VMPS_ERR_ALIGNMENT,
+                "%s: pool/q/k/v must be 16-byte aligned and q/k/v row strides multiples of 8 "
+                "elements",
+                what);
+  }
+  if (q_stride < static_cast<int64_t>(n_q) * head_dim ||
+      (fused && (k_stride < static_cast<int64_t>(n_kv) * head_dim ||
+                 v_stride < static_cast<int64_t>(n_kv) * head_dim))) {
+    return fail(VMPS_ERR_INVALID_ARG, "%s: row stride smaller than a row", what);
   }
   if (!(scale > 0.f) || !(scale < 1e30f)) {
-    return fail(VMPS_ERR_INVALID_ARG, "paged_decode_attention: scale %g", (double)scale);
+    return fail(VMPS_ERR_INVALID_ARG, "%s: scale %g", what, (double)scale);
   }
   int sms = 0;
   if (int rc = device_sm_count(&sms)) return rc;
   const int n_cta = sms * kCtasPerSm;
-  const size_t need = workspace_bytes(num_seqs, n_kv, head_dim, cfg, n_cta);
-  if (!workspace || workspace_bytes_given < need) {
-    return fail(VMPS_ERR_WORKSPACE, "paged_decode_attention: workspace %zu bytes < %zu needed",
-                workspace_bytes_given, need);
+  const WorkspaceLayout wl = workspace_layout(num_seqs, n_kv, head_dim, cfg, n_cta);
+  if (!workspace || workspace_bytes_given < wl.total) {
+    return fail(VMPS_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu needed", what,
+                workspace_bytes_given, wl.total);
   }
   if (reinterpret_cast<uintptr_t>(workspace) & 255) {
-    return fail(VMPS_ERR_ALIGNMENT, "paged_decode_attention: workspace must be 256-byte aligned");
+    return fail(VMPS_ERR_ALIGNMENT, "%s: workspace must be 256-byte aligned", what);
   }
   int* err = nullptr;
   if (int rc = device_error_word(&err)) return rc;
@@ -672,14 +1015,22 @@ static int decode_enqueue(void* out, const void* q, const void* pool, const int3
   if (int rc = encode_tiled(&tmap,
                             dtype == VMPS_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                     : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                            4, const_cast<void*>(pool), dims, strides, box,
-                            CU_TENSOR_MAP_SWIZZLE_128B)) {
+                            4, pool, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) {
     return rc;
   }
 
   DecodeParams p;
   p.out = out;
   p.q = q;
+  p.q_stride = q_stride;
+  p.k = k;
+  p.k_stride = k_stride;
+  p.v = v;
+  p.v_stride = v_stride;
+  p.positions = positions;
+  p.slot_mapping = slot_mapping;
+  p.inv_freq = inv_freq;
+  p.pool = pool;
   p.block_tables = block_tables;
   p.seq_lens = seq_lens;
   p.max_blocks = max_blocks_per_seq;
@@ -691,19 +1042,46 @@ static int decode_enqueue(void* out, const void* q, const void* pool, const int3
   p.num_hg = n_kv / cfg.hpc;
   p.n_cta = n_cta;
   p.scale_log2 = scale * 1.4426950408889634f;
-  const WorkspaceLayout wl = workspace_layout(num_seqs, head_dim, cfg, n_cta);
+  p.fused = fused;
+  p.early_prologue = fused;  // the fused step's seq_lens never come from the kernel before it
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  p.meta = reinterpret_cast<int*>(ws + wl.meta);
+  p.counters = reinterpret_cast<int*>(ws + wl.counters);
   p.part_ml = reinterpret_cast<float*>(ws + wl.ml);
   p.part_o = reinterpret_cast<float*>(ws + wl.o);
   p.err = err;
-  p.early_prologue = early_prologue;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return dtype == VMPS_DTYPE_F16 ? dispatch_decode<__half>(cfg, head_dim, tmap, p, s)
                                  : dispatch_decode<__nv_bfloat16>(cfg, head_dim, tmap, p, s);
 }
 
 }  // namespace vmps
+
+extern "C" size_t vmps_paged_decode_workspace_bytes(int num_seqs, int n_q, int n_kv, int head_dim,
+                                                    int dtype) {
+  using namespace vmps;
+  DecodeConfig cfg;
+  if (num_seqs < 0 || (dtype != VMPS_DTYPE_F16 && dtype != VMPS_DTYPE_BF16) ||
+      !pick_config(n_q, n_kv, head_dim, &cfg)) {
+    return 0;
+  }
+  int sms = 0;
+  if (device_sm_count(&sms)) return 0;
+  return workspace_layout(num_seqs > 0 ? num_seqs : 1, n_kv, head_dim, cfg, sms * kCtasPerSm)
+      .total;
+}
+
+extern "C" int vmps_paged_decode_workspace_init(void* workspace, size_t workspace_bytes,
+                                                void* stream) {
+  using namespace vmps;
+  clear_error();
+  if (!workspace && workspace_bytes) return fail(VMPS_ERR_INVALID_ARG, "workspace is NULL");
+  if (cudaMemsetAsync(workspace, 0, workspace_bytes, static_cast<cudaStream_t>(stream)) !=
+      cudaSuccess) {
+    return fail(VMPS_ERR_CUDA, "workspace memset failed: %s",
+                cudaGetErrorString(cudaGetLastError()));
+  }
+  return VMPS_OK;
+}
 
 extern "C" int vmps_paged_decode_attention(void* out, const void* q, const void* pool,
                                            const int32_t* block_tables, int max_blocks_per_seq,
@@ -712,9 +1090,11 @@ extern "C" int vmps_paged_decode_attention(void* out, const void* q, const void*
                                            int num_blocks, float scale, void* workspace,
                                            size_t workspace_bytes, int dtype, void* stream) {
   vmps::clear_error();
-  return vmps::decode_enqueue(out, q, pool, block_tables, max_blocks_per_seq, seq_lens, num_seqs,
-                              n_q, n_kv, head_dim, block_size, num_blocks, scale, workspace,
-                              workspace_bytes, dtype, stream, /*early_prologue=*/0);
+  return vmps::decode_enqueue(out, q, static_cast<int64_t>(n_q) * head_dim, nullptr, 0, nullptr,
+                              0, nullptr, nullptr, nullptr, const_cast<void*>(pool), block_tables,
+                              max_blocks_per_seq, seq_lens, num_seqs, n_q, n_kv, head_dim,
+                              block_size, num_blocks, scale, workspace, workspace_bytes, dtype,
+                              stream, /*fused=*/0, "paged_decode_attention");
 }
 
 extern "C" int vmps_paged_decode_step(void* out, void* q, int64_t q_row_stride, const void* k,
@@ -726,25 +1106,10 @@ extern "C" int vmps_paged_decode_step(void* out, void* q, int64_t q_row_stride, 
                                       int head_dim, int block_size, int num_blocks, float scale,
                                       void* workspace, size_t workspace_bytes, int dtype,
                                       void* stream) {
-  using namespace vmps;
-  clear_error();
-  if (q_row_stride != static_cast<int64_t>(n_q) * head_dim) {
-    return fail(VMPS_ERR_INVALID_ARG,
-                "paged_decode_step: q must be packed [num_seqs][n_q][head_dim] (row stride %lld)",
-                (long long)q_row_stride);
-  }
-  // Validate the attention arguments before anything is enqueued.
-  DecodeConfig cfg;
-  if (num_seqs > 0 && (block_size != kPageTokens || !pick_config(n_q, n_kv, head_dim, &cfg))) {
-    return fail(VMPS_ERR_UNSUPPORTED,
-                "paged_decode_step: n_q=%d n_kv=%d head_dim=%d block_size=%d not supported", n_q,
-                n_kv, head_dim, block_size);
-  }
-  int rc = vmps_rope_reshape_and_cache(q, q, q_row_stride, k, k_row_stride, v, v_row_stride,
-                                       positions, slot_mapping, inv_freq, pool, num_seqs, n_q,
-                                       n_kv, head_dim, block_size, num_blocks, dtype, stream);
-  if (rc) return rc;
-  return decode_enqueue(out, q, pool, block_tables, max_blocks_per_seq, seq_lens, num_seqs, n_q,
-                        n_kv, head_dim, block_size, num_blocks, scale, workspace, workspace_bytes,
-                        dtype, stream, /*early_prologue=*/1);
+  vmps::clear_error();
+  return vmps::decode_enqueue(out, q, q_row_stride, k, k_row_stride, v, v_row_stride, positions,
+                              slot_mapping, inv_freq, pool, block_tables, max_blocks_per_seq,
+                              seq_lens, num_seqs, n_q, n_kv, head_dim, block_size, num_blocks,
+                              scale, workspace, workspace_bytes, dtype, stream, /*fused=*/1,
+                              "paged_decode_step");
 }

@@ -11,21 +11,25 @@
 //
 // Limits and sharing rules:
 //   * The scratch is one file-scope device array of kNoAllocScratchBytes
-//     (16 MiB).  Every GPU on which the library's kernels are loaded holds
+//     (8 MiB).  Every GPU on which the library's kernels are loaded holds
 //     it until the process exits.
 //   * A call whose workspace would exceed it (see
 //     vmps_paged_decode_workspace_bytes) is rejected with
-//     VMPS_ERR_WORKSPACE before anything is launched.  On a 148-SM B200
-//     every supported shape with up to 4096 sequences fits (the largest,
-//     head_dim 64 with 16 query heads per kv head, needs ~14.6 MB).
+//     VMPS_ERR_WORKSPACE before anything is launched.  On a 148-SM B200 this
+//     admits every supported shape with up to 8 query heads per kv head
+//     (~6 MB: 1 MiB of merge counters plus the split-K partials of the
+//     grid) and rejects 16 query heads per kv head (~10.8 MB).
 //   * All calls on a device share the array and it keeps the last call's
-//     contents.  Nothing in it has to start at zero: each call writes the
-//     work split and the partial results before reading them.  Calls whose
-//     kernels may overlap on the GPU (different streams without ordering)
-//     race on the array and must not be issued.
+//     contents.  Its merge counters must start at zero: the first call on a
+//     device clears the whole array (cudaMemsetAsync on the caller's stream,
+//     not an allocation), and every call leaves the counters at zero again;
+//     the partial results are always written before they are read.  Calls
+//     whose kernels may overlap on the GPU (different streams without
+//     ordering) race on the array and must not be issued.
 //   * The first call on a device resolves the array's device address with
-//     cudaGetSymbolAddress (with that device current) and caches it; make
-//     that first call before any stream capture on the device.
+//     cudaGetSymbolAddress (with that device current), caches it and clears
+//     the array; make that first call before any stream capture on the
+//     device.
 //   * Nothing here calls cudaMalloc, cudaFree or any allocating routine.
 #include <mutex>
 
@@ -33,14 +37,14 @@
 
 namespace vmps {
 
-constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
 
 static __device__ __align__(256) uint8_t g_decode_scratch[kNoAllocScratchBytes];
 
 // Device address of g_decode_scratch on the current device.  The name is a
 // host-side stand-in in host code; only this address may be given to a
-// kernel.
-static int noalloc_scratch(void** out) {
+// kernel.  The first use on a device also clears the array on `stream`.
+static int noalloc_scratch(void** out, cudaStream_t stream) {
   static void* cached[64];
   static int status[64];
   static std::once_flag flags[64];
@@ -50,13 +54,14 @@ static int noalloc_scratch(void** out) {
   }
   std::call_once(flags[dev], [&] {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e == cudaSuccess) e = cudaMemsetAsync(p, 0, kNoAllocScratchBytes, stream);
     status[dev] = static_cast<int>(e);
     cached[dev] = (e == cudaSuccess) ? p : nullptr;
   });
   if (!cached[dev]) {
     return fail(VMPS_ERR_CUDA,
-                "paged_decode_attention_noalloc: cudaGetSymbolAddress of the scratch array "
+                "paged_decode_attention_noalloc: resolving or clearing the scratch array "
                 "failed: %s",
                 cudaGetErrorString(static_cast<cudaError_t>(status[dev])));
   }
@@ -95,7 +100,7 @@ extern "C" int vmps_paged_decode_attention_noalloc(void* out, const void* q, con
                 need, kNoAllocScratchBytes);
   }
   void* scratch = nullptr;
-  if (int rc = noalloc_scratch(&scratch)) return rc;
+  if (int rc = noalloc_scratch(&scratch, static_cast<cudaStream_t>(stream))) return rc;
   return vmps_paged_decode_attention(out, q, pool, block_tables, max_blocks_per_seq, seq_lens,
                                      num_seqs, n_q, n_kv, head_dim, block_size, num_blocks, scale,
                                      scratch, kNoAllocScratchBytes, dtype, stream);

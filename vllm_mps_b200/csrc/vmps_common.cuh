@@ -24,6 +24,7 @@ enum DevErr : int {
   kDevErrSeqLen = 4,         // seq_len needs more pages than max_blocks_per_seq
   kDevErrTimeout = 8,        // an mbarrier wait gave up
   kDevErrPositionRange = 16, // negative position
+  kDevErrSlotNotLast = 32,   // fused step: new-token slot not in the sequence's last page
 };
 
 __device__ __forceinline__ void set_error(int* err, int bit) {

@@ -215,9 +215,10 @@ def rope_reshape_and_cache(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 
 class DecodeWorkspace:
-    """Scratch buffer for :func:`paged_decode_attention`, grown on demand.
+    """Zero-initialised scratch for the decode kernels, grown on demand.
 
-    Holds the split-K partial results of one call; one buffer is reused
+    Holds the split-K partial results and per-sequence arrival counters of
+    one call; the kernel leaves the counters at zero, so one buffer is reused
     across calls on the same stream.  Calls on different streams that may
     overlap need different workspaces.
     """
@@ -237,7 +238,7 @@ class DecodeWorkspace:
         if buf is None or buf.numel() < need:
             # Grow geometrically; torch allocations are 512-byte aligned.
             size = max(need, 0 if buf is None else 2 * buf.numel())
-            buf = torch.empty(size, dtype=torch.uint8, device=device)
+            buf = torch.zeros(size, dtype=torch.uint8, device=device)
             self._buf[device] = buf
         return buf
 
@@ -295,16 +296,20 @@ def paged_decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                       block_tables: torch.Tensor, seq_lens: torch.Tensor,
                       scale: float | None = None, out: torch.Tensor | None = None,
                       workspace: DecodeWorkspace | torch.Tensor | None = None) -> torch.Tensor:
-    """One decode step of one layer: RoPE + cache write, then paged attention.
+    """One decode step of one layer in one kernel: RoPE, K/V write, paged attention.
 
-    ``q`` (B, n_q, D) contiguous is rotated in place; ``k``/``v`` (B, n_kv, D)
-    (any row stride) are written to ``pool`` at ``slot_mapping``.  Returns the
-    attention output (B, n_q, D).  Replaces PagedAttentionLayer._forward_batch
-    between its projections (layers/paged_attention_layer.py:275-359).
+    ``q`` (B, n_q, D) is rotated in registers (left unchanged in memory);
+    ``k``/``v`` (B, n_kv, D) (any row stride) are rotated / written to
+    ``pool`` at ``slot_mapping``, which must address position ``seq_lens-1``
+    of each sequence (its last page).  Returns the attention output
+    (B, n_q, D).  Replaces PagedAttentionLayer._forward_batch between its
+    projections (layers/paged_attention_layer.py:275-359).
     """
     num_blocks, block_size, n_kv, D = _check_pool(pool)
-    if q.dim() != 3 or q.shape[2] != D or not q.is_contiguous():
-        raise ValueError(f"q must be contiguous (B, n_q, {D})")
+    if q.dim() == 2:
+        q = q.view(q.shape[0], -1, D)
+    if q.dim() != 3 or q.shape[2] != D or q.stride(2) != 1 or q.stride(1) != D:
+        raise ValueError(f"q must be (B, n_q, {D}) with packed heads")
     B, n_q = q.shape[0], q.shape[1]
     ks = _rows(k, n_kv, D, "k")
     vs = _rows(v, n_kv, D, "v")
@@ -320,7 +325,7 @@ def paged_decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if inv_freq is not None and (inv_freq.dtype != torch.float32 or inv_freq.numel() != D // 2):
         raise ValueError(f"inv_freq must be float32 of {D // 2} entries")
     if out is None:
-        out = torch.empty_like(q)
+        out = torch.empty((B, n_q, D), dtype=q.dtype, device=q.device)
     dev = _require_cuda(q, k, v, positions, slot_mapping, inv_freq, pool, block_tables,
                         seq_lens, out)
     if scale is None:
