@@ -27,7 +27,8 @@ What is captured
 * ``engine_c0.npz`` -- config 0 end to end: the TinyLlama-shaped random
   fp16 model (seed 0), 8 prompts x 32 ids, 20 greedy steps through the
   reference engine (engine/llm_engine.py:316-346); tokens plus the top-5
-  logits of every decision.  (Needs ~2 min of CPU; ``--skip-engine``.)
+  logits of every decision, and the shared pool's used blocks at the start
+  of decisions 5 and 14.  (Needs ~2 min of CPU; ``--skip-engine``.)
 
 Usage::
 
@@ -275,14 +276,15 @@ def gen_slots_trace():
         else:
             continue
         if m.get_num_free_gpu_blocks() == 0 and rng.random() < 0.5:
-            # Keep the stream going: release the oldest live sequence.
-            s = live.pop(0)
-            m.free(s)
+            # Keep the stream going: record this op, then release the oldest
+            # live sequence as an op of its own.
             ops.append(op)
             args.append(a)
             snap = {q: m.get_block_table(q) for q in sorted(m.get_all_seq_ids())}
             tables_out.append(repr(snap))
             free_out.append((m.get_num_free_gpu_blocks(), m.get_num_free_cpu_blocks()))
+            s = live.pop(0)
+            m.free(s)
             op, a = "free", (s, -1)
         ops.append(op)
         args.append(a)
@@ -366,6 +368,12 @@ def c0_llama_config():
     )
 
 
+# Decisions of the config-0 run at whose start the pool is recorded: a
+# restart point for one-step checks (the shared-pool trace amplifies rounding
+# differences from step to step, so later steps are compared from here).
+C0_SNAP_STEPS = (5, 14)
+
+
 def gen_engine_c0(pal):
     """Config 0 through the reference engine, CPU fp16, greedy, 20 steps."""
     import torch
@@ -431,7 +439,16 @@ def gen_engine_c0(pal):
     top_vals, top_ids, step_seqs = [], [], []
     orig = adapter.forward_batch
 
+    snaps = {}
+
     def wrapped(token_ids, seq_ids, positions, seq_lens):
+        step = len(top_vals)
+        if step in C0_SNAP_STEPS:
+            # Pool contents at the start of this decision (before any layer
+            # writes), restricted to the blocks the running sequences own.
+            ids = sorted({b for sid in seq_ids for b in kv.get_block_table(sid)})
+            snaps[step] = (np.array(ids, dtype=np.int64),
+                           pool._pool[ids].contiguous().view(torch.int16).numpy().view(np.uint16))
         logits = orig(token_ids, seq_ids, positions, seq_lens)
         v, i = torch.topk(logits.float(), 5, dim=-1)
         top_vals.append(v.numpy())
@@ -453,6 +470,9 @@ def gen_engine_c0(pal):
         top_vals=np.stack(top_vals), top_ids=np.stack(top_ids),
         step_seqs=np.array(step_seqs, dtype=np.int64),
         cpu_seconds=dt, cpu_threads=torch.get_num_threads(),
+        snap_steps=np.array(sorted(snaps), dtype=np.int64),
+        **{f"snap{t}_blocks": snaps[t][0] for t in snaps},
+        **{f"snap{t}_pool": snaps[t][1] for t in snaps},
     )
     print(f"engine_c0: {steps} steps, {tokens.size} tokens in {dt:.2f}s")
 

@@ -1,0 +1,165 @@
+"""Host-side API that needs no GPU: the C-ABI library, the pool API, metadata, sampling.
+
+* The shared library loads here (it links no libcuda) and exports every
+  function ``include/vmps.h`` declares; host-side argument checks return
+  the documented status codes before any CUDA call.
+* The pool keeps the reference's layout, method set and ``IndexError``
+  bounds checks (memory/mps_memory_pool.py:82-268; the reference's
+  tests/test_memory_pool.py cases).
+* Step metadata (block tables, slot mapping) matches the reference's
+  addressing (models/llama_adapter.py:175-196).
+* Greedy sampling picks the first index on ties (model/sampler.py:33-34).
+"""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "vmps.h")
+
+
+def _declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\*?\s+\*?(vmps_[a-z_0-9]+)\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    from vllm_mps_b200 import kernels as K
+
+    lib = K.load_library()
+    declared = _declared_functions()
+    assert "vmps_paged_decode_step" in declared and len(declared) >= 8
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert set(K.EXPORTED_SYMBOLS) <= set(declared)
+    assert lib.vmps_version().startswith(b"vmps")
+
+
+def test_host_side_argument_checks_need_no_gpu():
+    from vllm_mps_b200 import kernels as K
+
+    lib = K.load_library()
+    # Bad dtype / sizes are rejected before any CUDA call.
+    rc = lib.vmps_rope_reshape_and_cache(None, None, 0, None, 0, None, 0, None, None, None, None,
+                                         4, 8, 2, 64, 16, 10, 7, None)
+    assert rc == -1 and b"dtype" in lib.vmps_last_error()
+    rc = lib.vmps_paged_decode_attention(None, None, None, None, 1, None, 4, 8, 2, 96, 16, 10,
+                                         0.1, None, 0, 0, None)
+    assert rc == -2  # head_dim 96 not built
+    rc = lib.vmps_paged_decode_attention(None, None, None, None, 1, None, 4, 8, 2, 64, 32, 10,
+                                         0.1, None, 0, 0, None)
+    assert rc == -2 and b"block_size" in lib.vmps_last_error()
+    rc = lib.vmps_paged_decode_attention(None, None, None, None, 1, None, 0, 8, 2, 64, 16, 10,
+                                         0.1, None, 0, 0, None)
+    assert rc == 0  # empty batch: nothing to do
+
+
+def test_kernel_wrappers_refuse_cpu_tensors():
+    from vllm_mps_b200 import kernels as K
+
+    pool = torch.zeros(4, 2, 16, 2, 64, dtype=torch.float16)
+    q = torch.zeros(1, 4, 64, dtype=torch.float16)
+    bt = torch.zeros(1, 1, dtype=torch.int32)
+    sl = torch.ones(1, dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        K.paged_decode_attention(q, pool, bt, sl)
+
+
+def test_pool_layout_and_reference_api_on_host():
+    from vllm_mps_b200.memory.mps_memory_pool import MPSMemoryPool
+
+    pool = MPSMemoryPool(8, 4, 2, 8, dtype=torch.float32, device="cpu")
+    assert list(pool._pool.shape) == [8, 2, 4, 2, 8]
+    k, v = torch.randn(2, 8), torch.randn(2, 8)
+    pool.write_kv(1, 3, k, v)
+    k1, v1 = pool.read_kv(1, 3)
+    assert torch.equal(k1, k) and torch.equal(v1, v)
+    for bid in (0, 1):
+        for pos in range(4):
+            pool.write_kv(bid, pos, torch.full((2, 8), float(bid * 4 + pos)),
+                          torch.full((2, 8), float(bid * 4 + pos + 100)))
+    kk, vv = pool.gather_blocks([0, 1])
+    assert kk.shape == (8, 2, 8) and torch.equal(kk[:, 0, 0], torch.arange(8.0))
+    assert torch.equal(vv[:, 1, 3], torch.arange(8.0) + 100)
+    pool.copy_block(0, 5)
+    assert torch.equal(pool.read_block_kv(5)[0], pool.read_block_kv(0)[0])
+    with pytest.raises(IndexError):
+        pool.write_kv(8, 0, k, v)
+    with pytest.raises(IndexError):
+        pool.write_kv(0, 4, k, v)
+    with pytest.raises(IndexError):
+        pool.copy_block(0, -1)
+    assert pool.get_memory_mb() > 0
+
+
+def test_per_layer_pool_and_swap_space_on_host():
+    from vllm_mps_b200.memory.cuda_memory_pool import CUDAMemoryPool, SwapSpace
+
+    pool = CUDAMemoryPool(6, 16, 2, 64, torch.float16, "cpu", num_layers=3)
+    assert pool.layer(2).shape == (6, 2, 16, 2, 64)
+    pool.layer(1)[2].fill_(3.0)
+    pool.layer(2)[2].fill_(5.0)
+    swap = SwapSpace(pool, 4)
+    swap.copy_out([2], [1])
+    pool._all.zero_()
+    swap.copy_in([1], [4])
+    assert float(pool.layer(1)[4].float().mean()) == 3.0
+    assert float(pool.layer(2)[4].float().mean()) == 5.0
+    pool.copy_block(4, 0)
+    assert float(pool.layer(2)[0].float().mean()) == 5.0
+
+
+def test_step_metadata_matches_reference_addressing():
+    from vllm_mps_b200.core.kv_cache_manager import KVCacheManager
+    from vllm_mps_b200.models.llama_adapter import build_step_metadata
+
+    kv = KVCacheManager(32, 4)
+    lens = [1, 16, 17, 40]
+    for sid, n in enumerate(lens):
+        kv.allocate(sid)
+        for _ in range(n):
+            kv.append_slot(sid)
+    meta = build_step_metadata(kv, list(range(4)), [n - 1 for n in lens], lens, 16,
+                               torch.device("cpu"))
+    tables = [kv.get_block_table(s) for s in range(4)]
+    assert meta.bt_tensor.shape == (4, 3)
+    for i, t in enumerate(tables):
+        assert meta.bt_tensor[i, :len(t)].tolist() == t
+        assert meta.bt_tensor[i, len(t):].eq(0).all()
+        p = lens[i] - 1
+        assert int(meta.slot_mapping[i]) == t[p // 16] * 16 + p % 16
+        assert meta.write_info[i].tolist() == [t[p // 16], p % 16]
+    assert meta.sl_tensor.tolist() == lens and meta.pos_tensor.tolist() == [n - 1 for n in lens]
+
+
+def test_greedy_sampler_takes_first_index_on_ties():
+    from vllm_mps_b200.core.sequence import SamplingParams
+    from vllm_mps_b200.model.sampler import Sampler
+
+    logits = torch.tensor([[0.0, 3.0, 3.0, 1.0], [5.0, 5.0, 5.0, 5.0]])
+    greedy = SamplingParams(temperature=0.0)
+    assert Sampler().sample_rows(logits, [greedy, greedy]) == [1, 0]
+    assert Sampler().sample(logits[0], greedy) == 1
+    g = torch.Generator().manual_seed(0)
+    tok = Sampler().sample_rows(logits, [SamplingParams(temperature=1.0, top_k=1), greedy], g)
+    # top-k keeps every logit >= the k-th largest (model/sampler.py:37-41): both 3.0s.
+    assert tok[0] in (1, 2) and tok[1] == 0
+
+
+def test_model_config_from_hf_config():
+    from transformers import LlamaConfig
+
+    from vllm_mps_b200.core.model_config import ModelConfig
+
+    hf = LlamaConfig(hidden_size=4096, num_attention_heads=32, num_key_value_heads=8,
+                     num_hidden_layers=32, vocab_size=128256, rope_theta=500000.0,
+                     max_position_embeddings=8192)
+    cfg = ModelConfig.from_hf_config(hf, "llama3-shape", device="cpu")
+    assert (cfg.n_heads, cfg.n_kv_heads, cfg.d_k, cfg.architecture) == (32, 8, 128, "llama")
+    assert cfg.rope_theta == 500000.0 and cfg.get_kv_cache_config()["n_heads"] == 8

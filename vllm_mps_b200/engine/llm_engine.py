@@ -1,0 +1,252 @@
+"""LLM inference engine (the reference's engine/llm_engine.py API on the B200 path).
+
+``LLMEngine.from_pretrained(name)`` / ``add_request`` / ``step`` /
+``generate`` / ``is_finished`` / ``get_tokens_per_sec`` keep the reference's
+contracts (engine/llm_engine.py:146-438).  ``from_model`` builds an engine
+around an in-memory HF model (random-init models in tests and benches).
+
+Two modes:
+
+* ``compat`` (default) reproduces the reference engine exactly: one KV pool
+  shared by every layer (engine/llm_engine.py:166-193) and no prefill -- a new
+  request reserves its prompt slots and only the last prompt token is fed
+  (:323-329), so earlier prompt slots are read as whatever the pool holds.
+  Greedy tokens then match the reference's.
+* ``physical``: one pool per layer and a real prefill of every prompt (and of
+  a resumed sequence whose K/V was not swapped), so attention sees the true
+  context.  ``swap=True`` also copies preempted blocks to pinned host memory
+  and back (the reference's swap moves metadata only).
+
+Per step the decode batch is one HF forward whose attention layers each run
+one fused sm_100a kernel; greedy sampling of the whole batch is one device
+argmax and one host copy.
+"""
+
+from __future__ import annotations
+
+import logging
+import time
+from dataclasses import dataclass, field
+
+import torch
+
+from vllm_mps_b200.config import BLOCK_SIZE, MAX_BATCH_SIZE, MAX_TOKENS_PER_STEP, NUM_CPU_BLOCKS, NUM_GPU_BLOCKS
+from vllm_mps_b200.core.kv_cache_manager import KVCacheManager
+from vllm_mps_b200.core.model_config import ModelConfig
+from vllm_mps_b200.core.sequence import SamplingParams, Sequence, SequenceGroup, SequenceStatus
+from vllm_mps_b200.engine.scheduler import Scheduler
+from vllm_mps_b200.memory.cuda_memory_pool import CUDAMemoryPool, SwapSpace
+from vllm_mps_b200.model.sampler import Sampler
+
+logger = logging.getLogger(__name__)
+
+
+@dataclass
+class RequestOutput:
+    """State of one request (engine/llm_engine.py:45-63)."""
+
+    request_id: int
+    prompt: str
+    generated_text: str = ""
+    token_ids: list[int] = field(default_factory=list)
+    finished: bool = False
+    num_steps: int = 0
+
+
+class LLMEngine:
+    """Scheduler + paged KV cache + HF model with paged attention layers."""
+
+    def __init__(self) -> None:
+        raise TypeError("use LLMEngine.from_pretrained(...) or LLMEngine.from_model(...)")
+
+    # ── construction ─────────────────────────────────────────────────────────
+
+    @classmethod
+    def from_pretrained(cls, model_name: str, sampling_params: SamplingParams | None = None,
+                        **kwargs) -> "LLMEngine":
+        """Load a HF model (hub name or local directory) and build the engine (:146-205)."""
+        from transformers import AutoModelForCausalLM, AutoTokenizer
+
+        cfg = ModelConfig.from_pretrained(model_name)
+        hf = AutoModelForCausalLM.from_pretrained(model_name, torch_dtype=cfg.dtype)
+        try:
+            tok = AutoTokenizer.from_pretrained(model_name)
+        except Exception:  # tokenizer files are optional
+            tok = None
+        return cls.from_model(hf, model_config=cfg, tokenizer=tok, model_name=model_name, **kwargs)
+
+    @classmethod
+    def from_model(cls, hf_model, model_config: ModelConfig | None = None, tokenizer=None,
+                   model_name: str = "model", num_gpu_blocks: int = NUM_GPU_BLOCKS,
+                   num_cpu_blocks: int = NUM_CPU_BLOCKS, max_batch_size: int = MAX_BATCH_SIZE,
+                   max_tokens_per_step: int = MAX_TOKENS_PER_STEP, mode: str = "compat",
+                   swap: bool = False, preempt_watermark: float | None = None,
+                   dtype: torch.dtype | None = None,
+                   device: torch.device | str | None = None) -> "LLMEngine":
+        from vllm_mps_b200.models.llama_adapter import LlamaAdapter
+
+        if mode not in ("compat", "physical"):
+            raise ValueError(f"mode must be 'compat' or 'physical', got {mode!r}")
+        cfg = model_config or ModelConfig.from_hf_config(hf_model.config, model_name, dtype, device)
+        if dtype is not None:
+            cfg.dtype = dtype
+        if device is not None:
+            cfg.device = torch.device(device)
+        pool = CUDAMemoryPool(num_gpu_blocks, BLOCK_SIZE, cfg.n_kv_heads, cfg.d_k, cfg.dtype,
+                              cfg.device, num_layers=cfg.n_layers if mode == "physical" else None)
+        swap_space = SwapSpace(pool, num_cpu_blocks) if swap else None
+        kv = KVCacheManager(num_gpu_blocks, num_cpu_blocks, swap_space=swap_space)
+
+        eng = cls.__new__(cls)
+        eng.mode = mode
+        eng.model_config = cfg
+        eng.memory_pool = pool
+        eng.kv_cache_manager = kv
+        eng.scheduler = Scheduler(kv, max_batch_size, max_tokens_per_step, preempt_watermark)
+        eng.sampler = Sampler()
+        eng.adapter = LlamaAdapter(model_name)
+        eng.adapter.attach(hf_model, cfg, kv, pool, tokenizer)
+        eng.tokenizer = tokenizer
+        eng._request_counter = 0
+        eng._outputs: dict[int, RequestOutput] = {}
+        eng._seq_to_request: dict[int, int] = {}
+        eng._seq_to_params: dict[int, SamplingParams] = {}
+        eng._seqs: dict[int, Sequence] = {}
+        eng._prefilled: set[int] = set()
+        eng.total_tokens_generated = 0
+        eng.start_time = time.time()
+        return eng
+
+    # ── requests ─────────────────────────────────────────────────────────────
+
+    def add_request(self, prompt: str | list[int], sampling_params: SamplingParams | None = None) -> int:
+        """Queue a request (text, or a list of token ids); returns its id (:247-282)."""
+        if sampling_params is None:
+            sampling_params = SamplingParams()
+        request_id = self._request_counter
+        self._request_counter += 1
+        if isinstance(prompt, str):
+            if self.tokenizer is None:
+                raise ValueError("text prompt given but the engine has no tokenizer")
+            token_ids, text = self.tokenizer.encode(prompt), prompt
+        else:
+            token_ids, text = [int(t) for t in prompt], ""
+        seq = Sequence(request_id, text, token_ids, sampling_params)
+        self.scheduler.add_request(SequenceGroup(request_id, [seq], sampling_params))
+        self._outputs[request_id] = RequestOutput(request_id=request_id, prompt=text)
+        self._seq_to_request[request_id] = request_id
+        self._seq_to_params[request_id] = sampling_params
+        self._seqs[request_id] = seq
+        return request_id
+
+    # ── stepping ─────────────────────────────────────────────────────────────
+
+    def step(self) -> list[RequestOutput]:
+        """One scheduling + decode step over every running sequence (:286-346)."""
+        sched_out = self.scheduler.schedule()
+        for group in sched_out.preempted_groups:
+            for s in group.sequences:
+                if self.kv_cache_manager.swap_space is None:
+                    self._prefilled.discard(s.seq_id)  # its K/V is gone
+        if not sched_out.scheduled_groups:
+            return []
+        seqs = [s for g in sched_out.scheduled_groups for s in g.get_seqs(SequenceStatus.RUNNING)]
+        if not seqs:
+            return []
+        if self.mode == "physical":
+            self._prefill([s for s in seqs if s.seq_id not in self._prefilled])
+        seq_ids = [s.seq_id for s in seqs]
+        token_ids = [s.get_last_token_id() for s in seqs]
+        positions = [s.get_total_len() - 1 for s in seqs]
+        seq_lens = [s.get_total_len() for s in seqs]
+        logits = self.adapter.forward_batch(token_ids, seq_ids, positions, seq_lens)
+        next_tokens = self.sampler.sample_rows(
+            logits, [self._seq_to_params.get(sid, SamplingParams()) for sid in seq_ids])
+        return self._update_sequences(seq_ids, next_tokens)
+
+    def _prefill(self, seqs: list[Sequence]) -> None:
+        """Write the K/V of every token but the last of each sequence, all layers.
+
+        All prompt tokens of all given sequences go through the model as one
+        batch of single-token rows.  Per layer, kernel 1 writes every row's
+        rotated K and V into its slot first, then the attention kernel runs
+        each row against its own prefix (seq_len = position + 1), so no row
+        reads a slot that is still being written.
+        """
+        from vllm_mps_b200.models import llama_adapter as la
+
+        rows_sid, rows_tok, rows_pos = [], [], []
+        for s in seqs:
+            hist = s.token_ids[:-1]
+            rows_sid += [s.seq_id] * len(hist)
+            rows_tok += hist
+            rows_pos += list(range(len(hist)))
+            self._prefilled.add(s.seq_id)
+        if not rows_tok:
+            return
+        dev = self.model_config.device
+        meta = la.build_step_metadata(self.kv_cache_manager, rows_sid, rows_pos,
+                                      [p + 1 for p in rows_pos], BLOCK_SIZE, dev)
+        tok = torch.tensor(rows_tok, dtype=torch.long, device=dev)
+        embeds = self.adapter.hf_model.model.embed_tokens(tok).unsqueeze(1)
+        ctx = la._batch_context
+        ctx.is_batch = True
+        ctx.prefill = True
+        ctx.seq_ids, ctx.positions, ctx.seq_lens = rows_sid, rows_pos, [p + 1 for p in rows_pos]
+        ctx.bt_tensor, ctx.sl_tensor, ctx.pos_tensor = meta.bt_tensor, meta.sl_tensor, meta.pos_tensor
+        ctx.slot_mapping, ctx.write_info = meta.slot_mapping, meta.write_info
+        try:
+            with torch.no_grad():
+                self.adapter.hf_model.model(inputs_embeds=embeds, use_cache=False)
+        finally:
+            ctx.is_batch = False
+            ctx.prefill = False
+
+    def _update_sequences(self, seq_ids: list[int], next_tokens: list[int]) -> list[RequestOutput]:
+        updated = []
+        for seq_id, token_id in zip(seq_ids, next_tokens):
+            request_id = self._seq_to_request.get(seq_id)
+            seq = self._seqs.get(seq_id)
+            if request_id is None or seq is None:
+                continue
+            seq.add_token(token_id)
+            self.total_tokens_generated += 1
+            if seq.is_finished():
+                self.scheduler.mark_finished(seq_id)
+                self._prefilled.discard(seq_id)
+                for pl in self.adapter.paged_layers:
+                    pl.evict_sequence(seq_id)
+            out = self._outputs[request_id]
+            out.token_ids = list(seq._output_token_ids)
+            if self.tokenizer is not None:
+                out.generated_text = self.tokenizer.decode(seq._output_token_ids,
+                                                           skip_special_tokens=True)
+            out.finished = seq.is_finished()
+            out.num_steps += 1
+            updated.append(out)
+        return updated
+
+    def generate(self, prompt: str | list[int], max_tokens: int = 50,
+                 temperature: float = 1.0) -> str | list[int]:
+        """Run one request to completion; text if a tokenizer is present, else ids (:387-417)."""
+        req = self.add_request(prompt, SamplingParams(max_tokens=max_tokens, temperature=temperature))
+        while not self._outputs[req].finished:
+            self.step()
+        out = self._outputs[req]
+        return out.generated_text if self.tokenizer is not None else list(out.token_ids)
+
+    def get_output(self, request_id: int) -> RequestOutput:
+        return self._outputs[request_id]
+
+    # ── queries ──────────────────────────────────────────────────────────────
+
+    def is_finished(self) -> bool:
+        return (self.scheduler.get_num_waiting() == 0 and self.scheduler.get_num_running() == 0
+                and self.scheduler.get_num_preempted() == 0)
+
+    def get_elapsed(self) -> float:
+        return time.time() - self.start_time
+
+    def get_tokens_per_sec(self) -> float:
+        elapsed = self.get_elapsed()
+        return 0.0 if elapsed == 0 else self.total_tokens_generated / elapsed
