@@ -80,7 +80,8 @@ def profile_traffic(cfg_name):
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
-                return int(line.split(":")[1].strip())
+                val = line.split(":")[1].strip()
+                return None if val == "null" else int(val)
     except OSError:
         pass
     return None
