@@ -1,0 +1,145 @@
+"""Sequence-sharded serving across the GPUs of one node.
+
+Decode and prefill have no dependency between sequences, so the engine
+shards requests, not tensors: every rank (one process per GPU, launched by
+torchrun) runs its own :class:`~vllm_mps_b200.engine.llm_engine.LLMEngine`
+with a full weight replica, its own KV pool and its own block allocator (the
+reference's single-device engine, engine/llm_engine.py:146-205, replicated).
+Block ids are rank-local, so each rank's slotting is exactly the reference's
+for the requests it owns.
+
+The only collective is one ``all_gather_into_tensor`` per step of a small
+int32 record per rank -- (global request id, sampled token, finished) for
+every sequence that produced a token, plus a "work left" flag -- used to
+assemble outputs on every rank and to end the loop on all ranks at the same
+step.  Over NCCL the record is a device tensor (NVLink/NVSwitch); over gloo
+(CPU tests) a host tensor.  Every rank takes the same number of collective
+steps, including ranks whose shard is already finished, so no rank waits on
+a collective the others never enter.
+"""
+
+from __future__ import annotations
+
+import heapq
+from dataclasses import dataclass, field
+
+import torch
+
+
+def shard_requests(costs: list[int], world: int) -> list[int]:
+    """Rank of every request: longest-first greedy balance of ``costs``.
+
+    ``costs[i]`` is the work of request i (prompt length + max new tokens).
+    Requests are taken in decreasing cost (ties: lower index first) and each
+    goes to the least-loaded rank (ties: lower rank), which keeps the largest
+    per-rank total within one request of the mean.  Deterministic, so every
+    rank computes the same assignment without communicating.
+    """
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    order = sorted(range(len(costs)), key=lambda i: (-costs[i], i))
+    heap = [(0, r) for r in range(world)]
+    owner = [0] * len(costs)
+    for i in order:
+        load, r = heapq.heappop(heap)
+        owner[i] = r
+        heapq.heappush(heap, (load + int(costs[i]), r))
+    return owner
+
+
+@dataclass
+class ShardedOutput:
+    """Tokens of one request as assembled from every rank's records."""
+
+    request_id: int
+    rank: int
+    token_ids: list[int] = field(default_factory=list)
+    finished: bool = False
+
+
+class ShardedEngine:
+    """Runs one engine per rank and gathers sampled tokens every step.
+
+    ``engine`` is this rank's engine (anything with ``add_request(prompt,
+    params) -> local id``, ``step() -> outputs with .request_id, .token_ids,
+    .finished``, ``is_finished()``).  ``capacity`` bounds the sequences one
+    rank reports per step (the engine's ``max_batch_size``); the record is
+    ``1 + 3 * capacity`` int32 per rank.
+    """
+
+    def __init__(self, engine, capacity: int, group=None, device: torch.device | None = None):
+        import torch.distributed as dist
+
+        self.engine = engine
+        self.capacity = int(capacity)
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        backend = dist.get_backend(group)
+        if device is None:
+            device = (torch.device("cuda", torch.cuda.current_device()) if backend == "nccl"
+                      else torch.device("cpu"))
+        self.device = device
+        self._local_to_global: dict[int, int] = {}
+        self.outputs: dict[int, ShardedOutput] = {}
+        self.steps = 0
+        self._rec = 1 + 3 * self.capacity
+        self._send = torch.empty(self._rec, dtype=torch.int32, device=device)
+        self._recv = torch.empty(self.world * self._rec, dtype=torch.int32, device=device)
+
+    def add_requests(self, prompts: list, params: list) -> list[int]:
+        """Shard ``prompts`` over the ranks; this rank queues its own share.
+
+        Global request ids are the indices into ``prompts``; every rank calls
+        this with the same lists.  Returns the owner rank of each request.
+        """
+        if len(prompts) != len(params):
+            raise ValueError("prompts and params differ in length")
+        costs = [len(p) + sp.max_tokens for p, sp in zip(prompts, params)]
+        owner = shard_requests(costs, self.world)
+        for gid, (p, sp) in enumerate(zip(prompts, params)):
+            self.outputs[gid] = ShardedOutput(request_id=gid, rank=owner[gid])
+            if owner[gid] == self.rank:
+                local = self.engine.add_request(p, sp)
+                self._local_to_global[local] = gid
+        return owner
+
+    def step(self) -> bool:
+        """One local engine step and the token gather; False once every rank is done."""
+        import torch.distributed as dist
+
+        produced = self.engine.step() if not self.engine.is_finished() else []
+        if len(produced) > self.capacity:
+            raise RuntimeError(f"rank {self.rank}: {len(produced)} sequences in one step "
+                               f"exceed the record capacity {self.capacity}")
+        rec = torch.full((self._rec,), -1, dtype=torch.int32)
+        rec[0] = 0 if self.engine.is_finished() else 1
+        for j, out in enumerate(produced):
+            rec[1 + 3 * j] = self._local_to_global[out.request_id]
+            rec[2 + 3 * j] = out.token_ids[-1]
+            rec[3 + 3 * j] = int(out.finished)
+        self._send.copy_(rec, non_blocking=False)
+        dist.all_gather_into_tensor(self._recv, self._send, group=self.group)
+        allrec = self._recv.view(self.world, self._rec).cpu()
+        more = False
+        for r in range(self.world):
+            row = allrec[r]
+            more |= bool(row[0] > 0)
+            for j in range(self.capacity):
+                gid = int(row[1 + 3 * j])
+                if gid < 0:
+                    break
+                o = self.outputs[gid]
+                if o.rank != r:
+                    raise RuntimeError(f"request {gid} reported by rank {r}, owned by {o.rank}")
+                o.token_ids.append(int(row[2 + 3 * j]))
+                o.finished = bool(row[3 + 3 * j])
+        self.steps += 1
+        return more
+
+    def run(self, max_steps: int | None = None) -> dict[int, ShardedOutput]:
+        """Step until every rank's shard is finished (or ``max_steps``)."""
+        while True:
+            more = self.step()
+            if not more or (max_steps is not None and self.steps >= max_steps):
+                return self.outputs
