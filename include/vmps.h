@@ -179,11 +179,42 @@ int vmps_paged_decode_attention_noalloc(void* out, const void* q, const void* po
                                         int dtype, void* stream);
 
 /*
+ * Causal paged prefill attention (kernel 3, tcgen05 tensor cores).  Replaces
+ * the reference's prompt processing, which runs the single-token path once
+ * per prompt token (layers/paged_attention_layer.py:175-241, driven by
+ * benchmarks/batch_size_benchmark.py:49-60): row r of sequence i sits at
+ * position q_start_pos[i] + r and attends to the sequence's slots
+ * 0..q_start_pos[i] + r, which must already hold K/V (written by
+ * vmps_rope_reshape_and_cache for the new rows).
+ *
+ * q:    [total_q rows][n_q][head_dim], rotated (kernel 1's q_out), row r of
+ *       sequence i at cu_q[i] + r; row stride q_row_stride elements
+ *       (multiple of 8).  16-byte aligned.
+ * out:  [total_q][n_q][head_dim], contiguous, same dtype; rows are written
+ *       only for r < q_lens[i].
+ * q_start_pos, q_lens, cu_q: int32 [num_seqs] on the device.  max_q_len
+ *       bounds q_lens (it sizes the grid; rows past it are not computed and
+ *       set error bit 64).
+ * block_tables: int32 [num_seqs][max_blocks_per_seq] covering
+ *       q_start_pos[i] + q_lens[i] slots.
+ * Supported: head_dim 64 or 128, block_size 16, n_q/n_kv in {1,2,4,8,16}.
+ * Allocates nothing; no workspace.
+ */
+int vmps_paged_prefill_attention(void* out, const void* q, int64_t q_row_stride,
+                                 const void* pool, const int32_t* block_tables,
+                                 int max_blocks_per_seq, const int32_t* q_start_pos,
+                                 const int32_t* q_lens, const int32_t* cu_q, int num_seqs,
+                                 int total_q, int max_q_len, int n_q, int n_kv, int head_dim,
+                                 int block_size, int num_blocks, float scale, int dtype,
+                                 void* stream);
+
+/*
  * Reads and clears the device error word of the current device (a bitwise OR
  * of index violations the kernels skipped since the last call).  Synchronises
  * `stream`.  Bits: 1 slot out of range, 2 block id out of range, 4 seq_len
  * beyond the block table, 8 an internal wait timed out, 16 negative position,
- * 32 a fused-step slot outside the sequence's last page.
+ * 32 a fused-step slot outside the sequence's last page, 64 prefill query
+ * rows outside [0, total_q) or a q_len above max_q_len.
  */
 int vmps_debug_error_word(void* stream, int* word_out);
 

@@ -203,3 +203,42 @@ def decode_step(q_bits, k_bits, v_bits, positions, seq_lens, block_tables, pool_
              nblk, block_size)
     out = paged_attention(q_rot, pool_bits, block_tables, seq_lens, dtype, block_size)
     return f32_to_bits(out, dtype), k_rot_bits
+
+
+def prefill_inputs(seed: int, rows: int, n_q: int, n_kv: int, D: int):
+    """Seeded float32 q/k/v of ``rows`` prefill rows (the fixtures' inputs)."""
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((rows, n_q, D), dtype=np.float32)
+    k = rng.standard_normal((rows, n_kv, D), dtype=np.float32)
+    v = rng.standard_normal((rows, n_kv, D), dtype=np.float32)
+    return q, k, v
+
+
+def prefill(q_bits, k_bits, v_bits, q_start, q_lens, block_tables, pool_bits, inv_freq,
+            dtype: str, block_size: int = 16):
+    """Causal prefill as the reference computes it: one token at a time.
+
+    Mirrors ``PagedAttentionLayer._forward_single`` (layers/paged_attention_layer.py:175-241)
+    called for every prompt token in order: rotate q and k at the token's
+    position, write k and v into the token's slot, attend to slots
+    ``0..position`` of the sequence.  Rows are laid out sequence after
+    sequence (``q_lens[i]`` rows of sequence i at positions
+    ``q_start[i] .. q_start[i] + q_lens[i] - 1``).  ``pool_bits`` is updated in
+    place.  Returns ``(out_bits (rows, n_q, D), k_rot_bits (rows, n_kv, D))``.
+    """
+    outs, ks = [], []
+    r = 0
+    for i, (qs, ql) in enumerate(zip(q_start, q_lens)):
+        for t in range(int(ql)):
+            pos = int(qs) + t
+            o, kr = decode_step(q_bits[r:r + 1], k_bits[r:r + 1], v_bits[r:r + 1], [pos],
+                                [pos + 1], [block_tables[i]], pool_bits, inv_freq, dtype,
+                                block_size)
+            outs.append(o[0])
+            ks.append(kr[0])
+            r += 1
+    n_q, D = q_bits.shape[1], q_bits.shape[2]
+    n_kv = k_bits.shape[1]
+    if not outs:
+        return (np.zeros((0, n_q, D), np.uint16), np.zeros((0, n_kv, D), np.uint16))
+    return np.stack(outs), np.stack(ks)

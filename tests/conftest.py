@@ -31,6 +31,17 @@ def golden_pool_bits(d) -> np.ndarray:
     return f32_to_bits(x, str(d["dtype"]))
 
 
+def prefill_fixture_inputs(d):
+    """q/k/v bits and pool of a ``prefill_*.npz`` fixture, regenerated from its seeds."""
+    from oracle.paged_attention_oracle import f32_to_bits, prefill_inputs
+
+    dt = str(d["dtype"])
+    rows = int(d["q_lens"].sum())
+    q, k, v = prefill_inputs(int(d["input_seed"]), rows, int(d["n_q"]), int(d["n_kv"]),
+                             int(d["D"]))
+    return f32_to_bits(q, dt), f32_to_bits(k, dt), f32_to_bits(v, dt), golden_pool_bits(d)
+
+
 @pytest.fixture(scope="session")
 def cuda_device():
     import torch

@@ -24,6 +24,10 @@ What is captured
 * ``sched_trace.npz`` -- a seeded request stream through the reference
   ``Scheduler`` (engine/scheduler.py:86-226): per step the scheduled
   sequence ids, the preempted groups and every block table.
+* ``prefill_*.npz`` -- prompt rows through the reference's single-token
+  path (layers/paged_attention_layer.py:175-241), token by token: the oracle
+  of the causal prefill kernel.  Inputs are regenerated from ``input_seed``
+  (``prefill_inputs``), the pool from ``pool_seed``.
 * ``engine_c0.npz`` -- config 0 end to end: the TinyLlama-shaped random
   fp16 model (seed 0), 8 prompts x 32 ids, 20 greedy steps through the
   reference engine (engine/llm_engine.py:316-346); tokens plus the top-5
@@ -213,6 +217,117 @@ def gen_attn_case(pal, case):
         sin_at_pos=rot.sin_cached[positions].numpy(),
     )
     print(f"{name}: B={B} ctx={list(map(int, ctx))[:6]}... written")
+
+
+# name, n_q, n_kv, D, dtype, [(q_start, q_len) per sequence], num_blocks, theta, max_pos, seed
+PREFILL_CASES = [
+    ("prefill_c1", 32, 4, 64, "float16", [(0, 37), (20, 30), (130, 6)], 40, 10000.0, 2048, 21),
+    ("prefill_c2", 16, 4, 128, "bfloat16", [(0, 33), (33, 12)], 24, 500000.0, 8192, 22),
+    ("prefill_mha", 4, 4, 64, "float16", [(0, 130), (7, 1)], 24, 10000.0, 2048, 23),
+    ("prefill_g16", 32, 2, 64, "float16", [(0, 24), (17, 9)], 16, 10000.0, 2048, 24),
+]
+
+
+def prefill_inputs(seed, rows, n_q, n_kv, D):
+    """Seeded float32 q/k/v of every prefill row (the tests regenerate them)."""
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((rows, n_q, D), dtype=np.float32)
+    k = rng.standard_normal((rows, n_kv, D), dtype=np.float32)
+    v = rng.standard_normal((rows, n_kv, D), dtype=np.float32)
+    return q, k, v
+
+
+def gen_prefill_case(pal, case):
+    """Prompt rows through the reference's single-token path, token by token.
+
+    ``_forward_single`` (layers/paged_attention_layer.py:175-241) writes the
+    token's rotated K and V into its slot, then attends to the sequence's
+    slots ``0..position`` -- per token, the causal prefill that kernel 3 does
+    for a whole prompt at once.  Sequence i already holds ``q_start`` tokens
+    (the seeded pool contents); its ``q_len`` new rows follow in order.
+    """
+    import torch
+    import torch.nn as nn
+    from vllm_mps.core.model_config import ModelConfig
+    from vllm_mps.memory.mps_memory_pool import MPSMemoryPool
+
+    (name, n_q, n_kv, D, dtn, seqs, nblk, theta, max_pos, seed) = case
+    dt = getattr(torch, dtn)
+    bs = 16
+    rng = np.random.default_rng(seed)
+    ctx = [qs + ql for qs, ql in seqs]
+    pages = [(c + bs - 1) // bs for c in ctx]
+    assert sum(pages) <= nblk, (name, pages, nblk)
+    perm = rng.permutation(nblk)
+    tables, off = [], 0
+    for p in pages:
+        tables.append([int(x) for x in perm[off: off + p]])
+        off += p
+    bt = np.zeros((len(seqs), max(pages)), dtype=np.int32)
+    for i, t in enumerate(tables):
+        bt[i, : len(t)] = t
+    rows = sum(ql for _, ql in seqs)
+    q32, k32, v32 = prefill_inputs(seed * 1000 + 1, rows, n_q, n_kv, D)
+    q_t, k_t, v_t = (torch.from_numpy(x).to(dt) for x in (q32, k32, v32))
+
+    pool_seed = seed * 1000 + 7
+    pshape = (nblk, 2, bs, n_kv, D)
+    pool_bits = pool_from_seed(pool_seed, pshape, dtn)
+    cfg = ModelConfig(
+        model_name="synthetic", architecture="llama", d_model=n_q * D,
+        n_heads=n_q, n_kv_heads=n_kv, d_k=D, n_layers=1, vocab_size=32000,
+        max_seq_len=max_pos, rope_theta=theta, dtype=dt, device=torch.device("cpu"),
+    )
+    pool = MPSMemoryPool(nblk, bs, n_kv, D, dt, torch.device("cpu"))
+    pool._pool.copy_(from_bits(pool_bits, dtn).view(pshape))
+
+    class _Tables:
+        def get_block_table(self, seq_id):
+            return tables[seq_id]
+
+    cur = {"row": 0}
+
+    class _Row(nn.Module):
+        def __init__(self, t, width):
+            super().__init__()
+            self.t, self.width = t, width
+
+        def forward(self, x):
+            return self.t[cur["row"]].reshape(1, 1, self.width)
+
+    outs = []
+
+    class _Capture(nn.Module):
+        def forward(self, x):
+            outs.append(x.detach().clone().reshape(n_q, D))
+            return x
+
+    rot = pal.RotaryEmbedding(D, max_pos, theta, torch.device("cpu"))
+    layer = pal.PagedAttentionLayer(
+        0, cfg, _Tables(), pool, _Row(q_t, n_q * D), _Row(k_t, n_kv * D), _Row(v_t, n_kv * D),
+        _Capture(), rot,
+    )
+    q_start = np.array([qs for qs, _ in seqs], dtype=np.int32)
+    q_lens = np.array([ql for _, ql in seqs], dtype=np.int32)
+    hidden = torch.zeros(1, 1, n_q * D, dtype=dt)
+    written_k = []
+    with torch.no_grad():
+        for i, (qs, ql) in enumerate(seqs):
+            for t in range(ql):
+                pos = qs + t
+                layer.set_context(i, pos)
+                layer._forward_single(hidden)
+                written_k.append(pool._pool[tables[i][pos // bs], 0, pos % bs].clone())
+                cur["row"] += 1
+    np.savez_compressed(
+        os.path.join(HERE, name + ".npz"),
+        n_q=n_q, n_kv=n_kv, D=D, dtype=dtn, block_size=bs, num_blocks=nblk,
+        theta=theta, max_pos=max_pos, pool_seed=pool_seed, input_seed=seed * 1000 + 1,
+        pool_sha256=hashlib.sha256(pool_bits.tobytes()).hexdigest(),
+        q_start=q_start, q_lens=q_lens, block_tables=bt,
+        written_k=to_bits(torch.stack(written_k)), attn_out=to_bits(torch.stack(outs)),
+    )
+    print(f"{name}: rows={rows} written")
 
 
 def gen_slots_trace():
@@ -487,6 +602,9 @@ def main():
     for case in ATTN_CASES:
         if not a.only or a.only in case[0]:
             gen_attn_case(pal, case)
+    for case in PREFILL_CASES:
+        if not a.only or a.only in case[0]:
+            gen_prefill_case(pal, case)
     if not a.only or a.only == "slots":
         gen_slots_trace()
     if not a.only or a.only == "sched":

@@ -12,7 +12,7 @@ import hashlib
 import numpy as np
 import pytest
 
-from conftest import golden_pool_bits, load_golden
+from conftest import golden_pool_bits, load_golden, prefill_fixture_inputs
 from oracle import c_oracle
 from oracle import paged_attention_oracle as O
 
@@ -118,3 +118,21 @@ def test_c_and_numpy_oracles_agree_on_a_ragged_batch():
     np.testing.assert_array_equal(p1, p2)
     np.testing.assert_allclose(O.bits_to_f32(o1, "float16"), O.bits_to_f32(o2, "float16"),
                                atol=2e-3, rtol=2e-3)
+
+
+PREFILL_FIXTURES = ["prefill_c1.npz", "prefill_c2.npz", "prefill_mha.npz", "prefill_g16.npz"]
+
+
+@pytest.mark.parametrize("name", PREFILL_FIXTURES)
+def test_prefill_oracle_matches_reference(name):
+    d = load_golden(name)
+    dt = str(d["dtype"])
+    q, k, v, pool = prefill_fixture_inputs(d)
+    assert hashlib.sha256(pool.tobytes()).hexdigest() == str(d["pool_sha256"])
+    out, kr = O.prefill(q, k, v, d["q_start"], d["q_lens"], d["block_tables"], pool,
+                        _inv_freq(d), dt)
+    np.testing.assert_array_equal(kr, d["written_k"])
+    atol, rtol = _tol(dt)
+    np.testing.assert_allclose(O.bits_to_f32(out, dt), O.bits_to_f32(d["attn_out"], dt),
+                               atol=atol, rtol=rtol)
+    assert (out == d["attn_out"]).mean() > 0.9

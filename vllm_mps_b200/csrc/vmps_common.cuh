@@ -25,6 +25,7 @@ enum DevErr : int {
   kDevErrTimeout = 8,        // an mbarrier wait gave up
   kDevErrPositionRange = 16, // negative position
   kDevErrSlotNotLast = 32,   // fused step: new-token slot not in the sequence's last page
+  kDevErrQueryRange = 64,    // prefill: q rows outside [0, total_q) or q_len > max_q_len
 };
 
 __device__ __forceinline__ void set_error(int* err, int bit) {
@@ -118,6 +119,15 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
       "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
 

@@ -50,6 +50,7 @@ EXPORTED_SYMBOLS = (
     "vmps_paged_decode_workspace_init",
     "vmps_paged_decode_attention",
     "vmps_paged_decode_step",
+    "vmps_paged_prefill_attention",
     "vmps_debug_error_word",
 )
 
@@ -90,6 +91,10 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.vmps_paged_decode_step.argtypes = [
             vp, vp, i64, vp, i64, vp, i64, vp, vp, vp, vp, vp, i32, vp,
             i32, i32, i32, i32, i32, i32, f32, vp, sz, i32, vp]
+        lib.vmps_paged_prefill_attention.restype = i32
+        lib.vmps_paged_prefill_attention.argtypes = [
+            vp, vp, i64, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32,
+            f32, i32, vp]
         lib.vmps_debug_error_word.restype = i32
         lib.vmps_debug_error_word.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
         if path is None:
@@ -343,6 +348,58 @@ def paged_decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
             float(scale), _ptr(ws), ws.numel() * ws.element_size(), dtype_code(pool.dtype),
             _stream(dev))
     _check(rc, "paged_decode_step")
+    return out
+
+
+# ── kernel 3 ─────────────────────────────────────────────────────────────────
+
+
+def paged_prefill_attention(q: torch.Tensor, pool: torch.Tensor, block_tables: torch.Tensor,
+                            q_start: torch.Tensor, q_lens: torch.Tensor, cu_q: torch.Tensor,
+                            max_q_len: int, scale: float | None = None,
+                            out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal attention of prompt rows over their sequences' paged K/V.
+
+    The whole-prompt form of the reference's token-by-token single-token
+    path (layers/paged_attention_layer.py:175-241): row r of sequence i is at
+    position ``q_start[i] + r`` and attends to slots ``0..q_start[i] + r``,
+    whose K/V must already be in ``pool`` (``rope_reshape_and_cache`` writes
+    the new rows').  ``q``: (total_q, n_q, D) rotated queries, heads packed
+    (rows may be strided); ``q_start``/``q_lens``/``cu_q``: int32 (B,) on the
+    device; ``max_q_len`` >= every ``q_lens`` entry (host int, sizes the
+    grid).  Returns ``out`` (total_q, n_q, D).
+    """
+    num_blocks, block_size, n_kv, D = _check_pool(pool)
+    if q.dim() == 2:
+        q = q.view(q.shape[0], -1, D)
+    if q.dim() != 3 or q.shape[2] != D or q.stride(2) != 1 or q.stride(1) != D:
+        raise ValueError(f"q must be (total_q, n_q, {D}) with packed heads; got {tuple(q.shape)}")
+    total_q, n_q = q.shape[0], q.shape[1]
+    B = q_lens.numel()
+    if block_tables.dim() != 2 or block_tables.shape[0] != B:
+        raise ValueError("block_tables must be (B, max_blocks)")
+    if q_start.numel() != B or cu_q.numel() != B:
+        raise ValueError("q_start, q_lens and cu_q must have one entry per sequence")
+    if q.dtype != pool.dtype:
+        raise TypeError(f"q dtype {q.dtype} != pool dtype {pool.dtype}")
+    for t, name in ((block_tables, "block_tables"), (q_start, "q_start"), (q_lens, "q_lens"),
+                    (cu_q, "cu_q")):
+        _int32(t, name)
+    if out is None:
+        out = torch.empty((total_q, n_q, D), dtype=q.dtype, device=q.device)
+    elif out.shape != (total_q, n_q, D) or out.dtype != q.dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous (total_q, n_q, D) tensor of q's dtype")
+    dev = _require_cuda(q, pool, block_tables, q_start, q_lens, cu_q, out)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    lib = load_library()
+    with torch.cuda.device(dev):
+        rc = lib.vmps_paged_prefill_attention(
+            _ptr(out), _ptr(q), q.stride(0), _ptr(pool), _ptr(block_tables),
+            block_tables.shape[1], _ptr(q_start), _ptr(q_lens), _ptr(cu_q), B, total_q,
+            int(max_q_len), n_q, n_kv, D, block_size, num_blocks, float(scale),
+            dtype_code(pool.dtype), _stream(dev))
+    _check(rc, "paged_prefill_attention")
     return out
 
 
