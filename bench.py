@@ -457,23 +457,223 @@ def run_ours(args, cfg, rank, world, local_rank):
     return 0
 
 
+# ── prefill (kernel 3) ───────────────────────────────────────────────────────
+
+PREFILL = {
+    # Llama-3-8B attention shape (config 2), bf16: 16 prompts of 2048 tokens, no cached prefix.
+    "prefill": (16, 2048, 32, 8, 128, "bfloat16", 500000.0,
+                "Causal paged prefill, Llama-3-8B attention shape: 16 prompts x 2048 tokens, "
+                "32 q / 8 kv heads, head_dim 128, bf16, block_size 16, permuted pool"),
+}
+
+
+def prefill_flops(B, L, n_q, D):
+    """QK^T and PV over the causal pairs: 4 * n_q * D per (row, key), L(L+1)/2 pairs per prompt."""
+    return B * (L * (L + 1) // 2) * 4 * n_q * D
+
+
+def prefill_cpu_baseline(B, L, n_q, n_kv, D, dt, theta, budget_s=10.0):
+    """C oracle on sampled prompt rows (the reference computes a prompt token by token).
+
+    Rows are taken at evenly spaced positions of one prompt, so their mean
+    cost is the mean cost of a prompt row; tokens/s = rows / time.
+    """
+    from oracle import c_oracle
+    from oracle.paged_attention_oracle import f32_to_bits, rope_inv_freq
+
+    c_oracle.build()
+    pages = (L + BLOCK - 1) // BLOCK
+    rng = np.random.default_rng(7)
+    pool = f32_to_bits(rng.standard_normal((pages, 2, BLOCK, n_kv, D), dtype=np.float32), dt)
+    table = np.arange(pages, dtype=np.int32)[None, :]
+    inv = rope_inv_freq(D, theta)
+    threads = os.cpu_count() or 1
+    q = f32_to_bits(rng.standard_normal((1, n_q, D), dtype=np.float32), dt)
+    k = f32_to_bits(rng.standard_normal((1, n_kv, D), dtype=np.float32), dt)
+    v = f32_to_bits(rng.standard_normal((1, n_kv, D), dtype=np.float32), dt)
+    order = np.random.default_rng(8).permutation(L)
+    c_oracle.decode_step(q, k, v, np.array([0]), np.array([1]), table, pool, inv, dt,
+                         threads=threads)
+    t0 = time.perf_counter()
+    n = 0
+    while n < L:
+        pos = int(order[n])
+        c_oracle.decode_step(q, k, v, np.array([pos]), np.array([pos + 1]), table, pool, inv,
+                             dt, threads=threads)
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    el = time.perf_counter() - t0
+    return {"value": n / el, "unit": "tokens/s", "cores": c_oracle.max_threads(), "kind": "port",
+            "sample": f"{n} rows at random positions of one {L}-token prompt in {el:.1f} s "
+                      f"(token-by-token, as the reference prefills), C oracle, OpenMP"}
+
+
+def run_prefill(args, rank, world, local_rank):
+    import torch
+
+    from vllm_mps_b200 import kernels as K
+    from vllm_mps_b200.layers.rotary_embedding import rope_inv_freq
+
+    B, L, n_q, n_kv, D, dtn, theta, desc = PREFILL[args.config]
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        base = prefill_cpu_baseline(B, L, n_q, n_kv, D, dtn, theta,
+                                    budget_s=max(3.0, 2.0 * (args.steps + args.warmup)))
+        v = base["value"]
+        print(json.dumps({
+            "metric": "prefill tokens/s", "value": v, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": B * L / v * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded)", "impl": "reference",
+            "config": {"workload": desc, "global_batch": B, "parallelism": "host cores"},
+            "cpu_baseline": base,
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return 0
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dt = getattr(torch, dtn)
+    pages = (L + BLOCK - 1) // BLOCK
+    nb = B * pages + 64
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    pool = torch.randn((nb, 2, BLOCK, n_kv, D), generator=g, device=dev, dtype=torch.float32).to(dt)
+    perm = torch.randperm(nb, device="cpu", generator=torch.Generator().manual_seed(rank))
+    bt = perm[: B * pages].view(B, pages).to(torch.int32).to(dev)
+    rows = B * L
+    q = torch.randn((rows, n_q, D), generator=g, device=dev, dtype=torch.float32).to(dt)
+    k = torch.randn((rows, n_kv, D), generator=g, device=dev, dtype=torch.float32).to(dt)
+    v = torch.randn((rows, n_kv, D), generator=g, device=dev, dtype=torch.float32).to(dt)
+    q_start = torch.zeros(B, dtype=torch.int32, device=dev)
+    q_lens = torch.full((B,), L, dtype=torch.int32, device=dev)
+    cu = torch.arange(0, rows, L, dtype=torch.int32, device=dev)
+    pos = torch.arange(L, dtype=torch.int32, device=dev).repeat(B)
+    seq = torch.arange(B, device=dev).repeat_interleave(L)
+    slots = (bt[seq, (pos // BLOCK).long()] * BLOCK + pos % BLOCK).to(torch.int32)
+    inv = rope_inv_freq(D, theta).to(dev)
+    out = torch.empty((rows, n_q, D), dtype=dt, device=dev)
+    q_rot = q.clone()
+    K.rope_reshape_and_cache(q, k, v, pos, slots, inv, pool, q_out=q_rot)
+
+    def attn():
+        K.paged_prefill_attention(q_rot, pool, bt, q_start, q_lens, cu, L, out=out)
+
+    for _ in range(args.warmup):
+        attn()
+    torch.cuda.synchronize(dev)
+    if K.error_word(dev):
+        raise RuntimeError("device error word set during warm-up")
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            attn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+    barrier()
+    t = max_over_ranks(e0.elapsed_time(e1) * 1e-3)
+
+    # End to end through the public API: host q/k/v in pinned memory, kernel 1
+    # (RoPE + K/V write) and kernel 3, output copied back, every step.
+    hq, hk, hv = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
+    hout = torch.empty_like(out, device="cpu").pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        K.rope_reshape_and_cache(dq, dk, dv, pos, slots, inv, pool)
+        K.paged_prefill_attention(dq, pool, bt, q_start, q_lens, cu, L, out=out)
+        hout.copy_(out, non_blocking=True)
+
+    e2e_steps = max(3, args.steps // 4)
+    for _ in range(3):
+        e2e()
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for _ in range(e2e_steps):
+        e2e()
+    e3.record()
+    torch.cuda.synchronize(dev)
+    barrier()
+    t_e2e = max_over_ranks(e2.elapsed_time(e3) * 1e-3)
+    if K.error_word(dev):
+        raise RuntimeError("device error word set during the timed region")
+    if rank == 0:
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peak, kind = float(json.load(f)["bf16_tflops"]), "measured (burst)"
+        except Exception:
+            peak, kind = 1590.0, "fallback"
+        flops = prefill_flops(B, L, n_q, D)
+        achieved = flops / (t / args.steps) / 1e12
+        line = {
+            "metric": "prefill tokens/s", "value": world * rows * args.steps / t,
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) q/k/v/pool)",
+            "config": {"workload": desc, "global_batch": B * world, "seq_len": L,
+                       "parallelism": f"sequence-sharded x{world}",
+                       "l2": "inputs larger than L2 (q 268 MB, out 268 MB, K/V 134 MB per rank)",
+                       "timing": "back-to-back launches, CUDA events, max over ranks"},
+            "e2e": {"value": world * rows * e2e_steps / t_e2e, "unit": "tokens/s",
+                    "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in (hq, hk, hv)),
+                    "d2h_bytes_per_step": hout.numel() * hout.element_size(),
+                    "api": "kernels.rope_reshape_and_cache + kernels.paged_prefill_attention, "
+                           "pinned host q/k/v"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None, "peak_kind": kind,
+                         "kernel": "paged_prefill_kernel",
+                         "kernel_us": t / args.steps * 1e6, "alg_flops_per_launch": flops},
+            "clocks": clocks.summary(),
+            "gpu_launches": args.steps,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = prefill_cpu_baseline(B, L, n_q, n_kv, D, dtn, theta)
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PREFILL), default="c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    cfg = CONFIGS[args.config]
+    cfg = CONFIGS.get(args.config)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
+    if args.impl == "reference" and cfg is not None:
         return run_reference(args, cfg, rank, world)
+    if args.impl == "reference":
+        return run_prefill(args, rank, world, local_rank)
     if world > 1:
         import torch
         import torch.distributed as dist
@@ -482,6 +682,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if cfg is None:
+            return run_prefill(args, rank, world, local_rank)
         return run_ours(args, cfg, rank, world, local_rank)
     finally:
         if world > 1:

@@ -117,7 +117,7 @@ def _init(rank, world, path, timeout_s=20):
 def _gather_worker(rank, world, path, result_dir):
     _init(rank, world, path)
     prompts, params = _workload()
-    eng = ShardedEngine(FakeEngine(batch=3), capacity=3)
+    eng = ShardedEngine(FakeEngine(batch=3))
     owner = eng.add_requests(prompts, params)
     outs = eng.run()
     res = {"owner": owner, "steps": eng.steps,
@@ -153,7 +153,7 @@ def test_gather_assembles_every_request_on_every_rank(world):
 def _oom_worker(rank, world, path, result_dir):
     _init(rank, world, path, timeout_s=5)
     prompts, params = _workload()
-    eng = ShardedEngine(FakeEngine(batch=3, fail_at_step=2 if rank == 1 else None), capacity=3)
+    eng = ShardedEngine(FakeEngine(batch=3, fail_at_step=2 if rank == 1 else None))
     eng.add_requests(prompts, params)
     outcome = "finished"
     try:

@@ -55,7 +55,7 @@ def _worker(rank, world, path, out_dir):
     eng = LLMEngine.from_model(_small_llama(), num_gpu_blocks=128, num_cpu_blocks=8,
                                max_batch_size=8, max_tokens_per_step=100000, mode="physical",
                                device=f"cuda:{rank}")
-    sharded = ShardedEngine(eng, capacity=8)
+    sharded = ShardedEngine(eng)
     prompts, params = _workload()
     owner = sharded.add_requests(prompts, params)
     outs = sharded.run()

@@ -145,7 +145,11 @@ def _hf_greedy(model, prompt, steps):
     return out_tokens, out_logits
 
 
-def test_physical_mode_prefill_matches_hf_attention():
+@pytest.mark.parametrize("max_prefill_rows", [8192, 16])
+def test_physical_mode_prefill_matches_hf_attention(max_prefill_rows):
+    """Kernel-3 prefill (whole prompts, or chunks of 16 rows that split
+    sequences and attend to earlier pieces through the pool) + decode steps
+    against HuggingFace's own eager attention over the full sequence."""
     import copy
 
     from vllm_mps_b200.core.sequence import SamplingParams
@@ -154,9 +158,10 @@ def test_physical_mode_prefill_matches_hf_attention():
     model = _small_llama()
     ref_model = copy.deepcopy(model).cuda()
     rng = np.random.default_rng(3)
-    prompts = [rng.integers(0, 1024, size=n).tolist() for n in (5, 23, 40, 1)]
+    prompts = [rng.integers(0, 1024, size=n).tolist() for n in (5, 23, 40, 1, 300)]
     eng = LLMEngine.from_model(model, num_gpu_blocks=64, num_cpu_blocks=8, max_batch_size=8,
-                               max_tokens_per_step=10000, mode="physical", device="cuda")
+                               max_tokens_per_step=10000, mode="physical", device="cuda",
+                               max_prefill_rows=max_prefill_rows)
     seen = []
     real_sample = eng.sampler.sample_rows
 

@@ -138,6 +138,32 @@ def test_step_metadata_matches_reference_addressing():
     assert meta.sl_tensor.tolist() == lens and meta.pos_tensor.tolist() == [n - 1 for n in lens]
 
 
+def test_prefill_metadata_rows_and_sequences():
+    from vllm_mps_b200.core.kv_cache_manager import KVCacheManager
+    from vllm_mps_b200.models.llama_adapter import build_prefill_metadata
+
+    kv = KVCacheManager(32, 4)
+    lens = [5, 40, 17]
+    for sid, n in enumerate(lens):
+        kv.allocate(sid)
+        for _ in range(n):
+            kv.append_slot(sid)
+    pieces = [(0, 0, 4), (1, 16, 23), (2, 0, 16)]  # sequence 1 resumes at position 16
+    meta = build_prefill_metadata(kv, pieces, 16, torch.device("cpu"))
+    tables = [kv.get_block_table(s) for s in range(3)]
+    assert meta.rows == 43 and meta.max_q_len == 23
+    assert meta.q_start.tolist() == [0, 16, 0] and meta.q_lens.tolist() == [4, 23, 16]
+    assert meta.cu_q.tolist() == [0, 4, 27]
+    for i, t in enumerate(tables):
+        assert meta.bt_tensor[i, :len(t)].tolist() == t
+    r = 0
+    for sid, qs, ql in pieces:
+        for p in range(qs, qs + ql):
+            assert int(meta.pos_tensor[r]) == p
+            assert int(meta.slot_mapping[r]) == tables[sid][p // 16] * 16 + p % 16
+            r += 1
+
+
 def test_greedy_sampler_takes_first_index_on_ties():
     from vllm_mps_b200.core.sequence import SamplingParams
     from vllm_mps_b200.model.sampler import Sampler

@@ -62,16 +62,24 @@ class ShardedEngine:
 
     ``engine`` is this rank's engine (anything with ``add_request(prompt,
     params) -> local id``, ``step() -> outputs with .request_id, .token_ids,
-    .finished``, ``is_finished()``).  ``capacity`` bounds the sequences one
-    rank reports per step (the engine's ``max_batch_size``); the record is
-    ``1 + 3 * capacity`` int32 per rank.
+    .finished``, ``is_finished()``).  The record of a rank holds ``1 + 3 *
+    capacity`` int32.  By default ``capacity`` is the largest number of
+    requests any rank owns (every rank computes the same value from the
+    shared assignment), which bounds the sequences a step can produce: the
+    reference's scheduler admits waiting requests before it counts the
+    running ones, so one step may schedule more than ``max_batch_size``
+    (engine/scheduler.py:127-187).  A smaller explicit ``capacity`` saves
+    bandwidth and is checked before every collective.
     """
 
-    def __init__(self, engine, capacity: int, group=None, device: torch.device | None = None):
+    def __init__(self, engine, capacity: int | None = None, group=None,
+                 device: torch.device | None = None):
         import torch.distributed as dist
 
         self.engine = engine
-        self.capacity = int(capacity)
+        self.capacity = None if capacity is None else int(capacity)
+        if self.capacity is not None and self.capacity < 1:
+            raise ValueError("capacity must be >= 1")
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -83,9 +91,18 @@ class ShardedEngine:
         self._local_to_global: dict[int, int] = {}
         self.outputs: dict[int, ShardedOutput] = {}
         self.steps = 0
+        self._rec = 0
+        self._send = self._recv = None
+
+    def _size_records(self, owner: list[int]) -> None:
+        if self.capacity is None:
+            counts = [0] * self.world
+            for r in owner:
+                counts[r] += 1
+            self.capacity = max(1, max(counts))
         self._rec = 1 + 3 * self.capacity
-        self._send = torch.empty(self._rec, dtype=torch.int32, device=device)
-        self._recv = torch.empty(self.world * self._rec, dtype=torch.int32, device=device)
+        self._send = torch.empty(self._rec, dtype=torch.int32, device=self.device)
+        self._recv = torch.empty(self.world * self._rec, dtype=torch.int32, device=self.device)
 
     def add_requests(self, prompts: list, params: list) -> list[int]:
         """Shard ``prompts`` over the ranks; this rank queues its own share.
@@ -95,8 +112,11 @@ class ShardedEngine:
         """
         if len(prompts) != len(params):
             raise ValueError("prompts and params differ in length")
+        if self._send is not None:
+            raise RuntimeError("add_requests may be called once per ShardedEngine")
         costs = [len(p) + sp.max_tokens for p, sp in zip(prompts, params)]
         owner = shard_requests(costs, self.world)
+        self._size_records(owner)
         for gid, (p, sp) in enumerate(zip(prompts, params)):
             self.outputs[gid] = ShardedOutput(request_id=gid, rank=owner[gid])
             if owner[gid] == self.rank:
@@ -108,6 +128,8 @@ class ShardedEngine:
         """One local engine step and the token gather; False once every rank is done."""
         import torch.distributed as dist
 
+        if self._send is None:
+            self._size_records([])
         produced = self.engine.step() if not self.engine.is_finished() else []
         if len(produced) > self.capacity:
             raise RuntimeError(f"rank {self.rank}: {len(produced)} sequences in one step "

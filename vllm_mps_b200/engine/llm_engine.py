@@ -82,7 +82,8 @@ class LLMEngine:
                    max_tokens_per_step: int = MAX_TOKENS_PER_STEP, mode: str = "compat",
                    swap: bool = False, preempt_watermark: float | None = None,
                    dtype: torch.dtype | None = None,
-                   device: torch.device | str | None = None) -> "LLMEngine":
+                   device: torch.device | str | None = None,
+                   max_prefill_rows: int = 8192) -> "LLMEngine":
         from vllm_mps_b200.models.llama_adapter import LlamaAdapter
 
         if mode not in ("compat", "physical"):
@@ -113,6 +114,9 @@ class LLMEngine:
         eng._seq_to_params: dict[int, SamplingParams] = {}
         eng._seqs: dict[int, Sequence] = {}
         eng._prefilled: set[int] = set()
+        if max_prefill_rows < 1:
+            raise ValueError("max_prefill_rows must be >= 1")
+        eng.max_prefill_rows = int(max_prefill_rows)
         eng.total_tokens_generated = 0
         eng.start_time = time.time()
         return eng
@@ -167,40 +171,52 @@ class LLMEngine:
     def _prefill(self, seqs: list[Sequence]) -> None:
         """Write the K/V of every token but the last of each sequence, all layers.
 
-        All prompt tokens of all given sequences go through the model as one
-        batch of single-token rows.  Per layer, kernel 1 writes every row's
-        rotated K and V into its slot first, then the attention kernel runs
-        each row against its own prefix (seq_len = position + 1), so no row
-        reads a slot that is still being written.
+        The prompt rows go through the model in chunks of at most
+        ``max_prefill_rows`` rows (a longer sequence is split, later pieces
+        attending to the earlier ones through the pool).  Per layer, kernel 1
+        writes every row's rotated K and V, then kernel 3 (tcgen05 causal
+        prefill) computes each row against its sequence's slots
+        ``0..position``.
         """
+        pieces, rows = [], 0
+        for s in seqs:
+            self._prefilled.add(s.seq_id)
+            n = len(s.token_ids) - 1
+            start = 0
+            while start < n:
+                take = min(n - start, self.max_prefill_rows - rows)
+                pieces.append((s, start, take))
+                rows += take
+                start += take
+                if rows == self.max_prefill_rows:
+                    self._prefill_chunk(pieces)
+                    pieces, rows = [], 0
+        if pieces:
+            self._prefill_chunk(pieces)
+
+    def _prefill_chunk(self, pieces) -> None:
         from vllm_mps_b200.models import llama_adapter as la
 
-        rows_sid, rows_tok, rows_pos = [], [], []
-        for s in seqs:
-            hist = s.token_ids[:-1]
-            rows_sid += [s.seq_id] * len(hist)
-            rows_tok += hist
-            rows_pos += list(range(len(hist)))
-            self._prefilled.add(s.seq_id)
-        if not rows_tok:
-            return
         dev = self.model_config.device
-        meta = la.build_step_metadata(self.kv_cache_manager, rows_sid, rows_pos,
-                                      [p + 1 for p in rows_pos], BLOCK_SIZE, dev)
-        tok = torch.tensor(rows_tok, dtype=torch.long, device=dev)
-        embeds = self.adapter.hf_model.model.embed_tokens(tok).unsqueeze(1)
+        meta = la.build_prefill_metadata(self.kv_cache_manager,
+                                         [(s.seq_id, qs, ql) for s, qs, ql in pieces],
+                                         BLOCK_SIZE, dev)
+        toks = [t for s, qs, ql in pieces for t in s.token_ids[qs:qs + ql]]
+        tok = torch.tensor(toks, dtype=torch.long)
+        if dev.type == "cuda":
+            tok = tok.pin_memory()
+        embeds = self.adapter.hf_model.model.embed_tokens(tok.to(dev, non_blocking=True)).unsqueeze(1)
         ctx = la._batch_context
         ctx.is_batch = True
         ctx.prefill = True
-        ctx.seq_ids, ctx.positions, ctx.seq_lens = rows_sid, rows_pos, [p + 1 for p in rows_pos]
-        ctx.bt_tensor, ctx.sl_tensor, ctx.pos_tensor = meta.bt_tensor, meta.sl_tensor, meta.pos_tensor
-        ctx.slot_mapping, ctx.write_info = meta.slot_mapping, meta.write_info
+        ctx.prefill_meta = meta
         try:
             with torch.no_grad():
                 self.adapter.hf_model.model(inputs_embeds=embeds, use_cache=False)
         finally:
             ctx.is_batch = False
             ctx.prefill = False
+            ctx.prefill_meta = None
 
     def _update_sequences(self, seq_ids: list[int], next_tokens: list[int]) -> list[RequestOutput]:
         updated = []

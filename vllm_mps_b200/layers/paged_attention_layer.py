@@ -117,12 +117,15 @@ class PagedAttentionLayer(nn.Module):
         return self.W_O(out.view(B, 1, n_q * D))
 
     def _prefill_rows(self, hidden_states: torch.Tensor, meta) -> torch.Tensor:
-        """Prompt rows: kernel 1 writes every row's K/V, then each row attends to its prefix.
+        """Prompt rows of a prefill chunk: kernel 1 writes every row's K/V, kernel 3 attends.
 
-        Two launches because rows of one sequence read each other's slots; the
-        decode-step kernel only makes a row's own new token visible to itself.
+        Kernel 1 rotates q in place inside the fused QKV output and writes the
+        rotated K and V of all rows into their slots; kernel 3 (tcgen05 causal
+        prefill) then computes every row against its sequence's slots
+        ``0..position`` -- the result of the reference's token-by-token
+        single-token path (:175-241) for the whole chunk at once.
         """
-        from vllm_mps_b200.kernels import paged_decode_attention, rope_reshape_and_cache
+        from vllm_mps_b200.kernels import paged_prefill_attention, rope_reshape_and_cache
 
         B = hidden_states.shape[0]
         n_q, n_kv, D = self.n_heads, self.n_kv_heads, self.d_k
@@ -132,9 +135,9 @@ class PagedAttentionLayer(nn.Module):
         v = qkv[:, (n_q + n_kv) * D:]
         rope_reshape_and_cache(q, k, v, meta.pos_tensor, meta.slot_mapping,
                                self.rotary_emb.inv_freq, self._pool())
-        out = paged_decode_attention(q.contiguous().view(B, n_q, D), self._pool(), meta.bt_tensor,
-                                     meta.sl_tensor, scale=1.0 / math.sqrt(D),
-                                     workspace=self._workspace_buf())
+        out = paged_prefill_attention(q.view(B, n_q, D), self._pool(), meta.bt_tensor,
+                                      meta.q_start, meta.q_lens, meta.cu_q, meta.max_q_len,
+                                      scale=1.0 / math.sqrt(D))
         return self.W_O(out.view(B, 1, n_q * D))
 
     def _forward_batch(self, hidden_states: torch.Tensor, seq_ids: list[int],
@@ -143,7 +146,7 @@ class PagedAttentionLayer(nn.Module):
         from vllm_mps_b200.models.llama_adapter import _batch_context
 
         if getattr(_batch_context, "prefill", False):
-            return (self._prefill_rows(hidden_states, _batch_context), None)
+            return (self._prefill_rows(hidden_states, _batch_context.prefill_meta), None)
         return (self._attend(hidden_states, _batch_context), None)
 
     def _forward_single(self, hidden_states: torch.Tensor):

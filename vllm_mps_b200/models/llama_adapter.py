@@ -39,6 +39,7 @@ _batch_context.sl_tensor = None      # int32 (B,)
 _batch_context.pos_tensor = None     # int32 (B,)
 _batch_context.slot_mapping = None   # int32 (B,): block_id * block_size + token_pos
 _batch_context.prefill = False       # rows are prompt tokens (engine prefill)
+_batch_context.prefill_meta = None   # build_prefill_metadata(...) of the prefill chunk
 
 
 def build_step_metadata(kv_cache_manager, seq_ids, positions, seq_lens, block_size: int,
@@ -72,6 +73,43 @@ def build_step_metadata(kv_cache_manager, seq_ids, positions, seq_lens, block_si
     )
     meta.write_info = torch.stack([meta.slot_mapping // block_size, meta.slot_mapping % block_size], 1)
     return meta
+
+
+def build_prefill_metadata(kv_cache_manager, pieces, block_size: int,
+                           device: torch.device) -> SimpleNamespace:
+    """Device metadata of one prefill chunk (one pinned host buffer, one copy).
+
+    ``pieces``: ``(seq_id, q_start, q_len)`` per sequence; the chunk's rows
+    are the ``q_len`` tokens at positions ``q_start ..`` of each sequence in
+    order.  Per row: position and slot (kernel 1 writes each row's K/V); per
+    sequence: block table, ``q_start``, ``q_len`` and first row ``cu_q``
+    (kernel 3 attends each row to its sequence's slots ``0..position``).
+    """
+    S = len(pieces)
+    tables = [kv_cache_manager.get_block_table(sid) for sid, _, _ in pieces]
+    max_blocks = max(1, max(len(t) for t in tables))
+    q_start = np.array([qs for _, qs, _ in pieces], dtype=np.int64)
+    q_lens = np.array([ql for _, _, ql in pieces], dtype=np.int64)
+    rows = int(q_lens.sum())
+    cu = np.zeros(S, dtype=np.int64)
+    cu[1:] = np.cumsum(q_lens)[:-1]
+    bt = np.zeros((S, max_blocks), dtype=np.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = t
+    seq_of_row = np.repeat(np.arange(S), q_lens)
+    pos = (np.arange(rows) - cu[seq_of_row] + q_start[seq_of_row]).astype(np.int64)
+    slots = bt[seq_of_row, pos // block_size].astype(np.int64) * block_size + pos % block_size
+    flat = np.concatenate([bt.reshape(-1), q_start, q_lens, cu, pos, slots]).astype(np.int32)
+    pinned = torch.from_numpy(flat)
+    if device.type == "cuda":
+        pinned = pinned.pin_memory()
+    dev = pinned.to(device, non_blocking=True)
+    o = S * max_blocks
+    return SimpleNamespace(
+        bt_tensor=dev[:o].view(S, max_blocks), q_start=dev[o:o + S], q_lens=dev[o + S:o + 2 * S],
+        cu_q=dev[o + 2 * S:o + 3 * S], pos_tensor=dev[o + 3 * S:o + 3 * S + rows],
+        slot_mapping=dev[o + 3 * S + rows:o + 3 * S + 2 * rows],
+        max_q_len=int(q_lens.max()) if S else 0, rows=rows)
 
 
 class LlamaAdapter(BaseModelAdapter):
