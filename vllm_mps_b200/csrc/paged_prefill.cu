@@ -11,7 +11,8 @@
 // Work split.  A CTA owns one 128-row tile of one kv head of one sequence.
 // The rows are (query token, query head) pairs: 128/G consecutive tokens x
 // the G query heads that share the kv head, so every K/V tile loaded serves
-// all G heads (GQA is never materialised).  Key tiles are 128 keys = 8 pages.
+// all G heads (GQA is never materialised).  Key tiles are 128 keys (8 pages)
+// for head_dim 64 and 64 keys for head_dim 128.
 //
 // Data movement.  Warp 4 (one lane) loads the Q tile with a 3-D TMA and the
 // K and V pages with 4-D TMAs (no multicast), all with the 128-byte swizzle,
@@ -19,10 +20,11 @@
 // are fetched at an out-of-range coordinate, which the TMA fills with zeros.
 //
 // Math.  Warp 5 (one lane) issues tcgen05.mma (kind::f16, M=128, fp32
-// accumulate): S = Q K^T into 128 TMEM columns, then O += P V into D more
+// accumulate): S = Q K^T into KEYS TMEM columns, then O += P V into D more
 // columns, P read from shared memory (K-major) and V as an MN-major operand,
 // so V needs no transpose.  Warps 0-3 own one row each (TMEM lane = row):
-// they load the row of S, apply the causal mask and the scale, keep the
+// they read the row of S twice (max, then exp2), apply the causal mask and
+// the scale, keep the
 // running max and sum in fp32 (rescaling O in TMEM only when the max grows
 // by more than 2^8, so most tiles skip it), write P = exp2(s - max) as 16-bit
 // values into the swizzled P tile, and finally normalise O and store it.
@@ -41,22 +43,26 @@ namespace vmps {
 namespace {
 
 constexpr int kPfRows = 128;       // MMA M: rows per tile
-constexpr int kPfKeys = 128;       // keys per key tile (8 pages of 16)
 constexpr int kPfStages = 2;       // K/V ring depth
 constexpr int kPfThreads = 192;    // warps 0-3 softmax, 4 loads, 5 MMA
-constexpr int kChunkBytes = 128 * 128;  // 128 rows x 64 16-bit columns (one swizzle span)
-constexpr uint32_t kTmemCols = 256;     // S: 128 columns, O: up to 128
+constexpr int kRegion = 128 * 128; // 128 rows x 64 16-bit columns (one swizzle span)
 
-template <int D>
+// KEYS = keys per key tile: 128 for head_dim 64, 64 for head_dim 128, so
+// that a CTA needs ~113 KB of shared memory and two CTAs share an SM (one's
+// softmax runs while the other's MMAs do).
+template <int D, int KEYS>
 struct PrefillShape {
   static constexpr int kChunks = D / 64;
-  static constexpr int kQBytes = kChunks * kChunkBytes;
-  static constexpr int kKBytes = kChunks * kChunkBytes;  // one key tile of K (or of V)
+  static constexpr int kPages = KEYS / 16;
+  static constexpr int kQBytes = kChunks * kRegion;
+  static constexpr int kKRegion = KEYS * 128;             // one 64-column chunk of a key tile
+  static constexpr int kKBytes = kChunks * kKRegion;      // K (or V) of one key tile
   static constexpr int kStageBytes = 2 * kKBytes;
-  static constexpr int kPBytes = (kPfKeys / 64) * kChunkBytes;
+  static constexpr int kPBytes = (KEYS / 64) * kRegion;
   static constexpr int kBarBytes = 128;
-  static constexpr int kSmemBytes =
-      1024 + kQBytes + kPfStages * kStageBytes + kPBytes + kBarBytes;
+  static constexpr int kSmemBytes = kQBytes + kPfStages * kStageBytes + kPBytes + kBarBytes;
+  // TMEM: S in columns [0, KEYS), O in [KEYS, KEYS + D); power of two >= 32.
+  static constexpr uint32_t kTmemCols = (KEYS + D <= 128) ? 128u : 256u;
 };
 
 struct PrefillParams {
@@ -157,14 +163,19 @@ __device__ __forceinline__ uint32_t f16_idesc(int n, bool b_mn_major) {
 
 __device__ __forceinline__ bool aborted(volatile int* flag) { return *flag != 0; }
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kPfThreads, 1)
+template <typename T, int D, int KEYS>
+__global__ void __launch_bounds__(kPfThreads, 2)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap kv_map,
                          const __grid_constant__ CUtensorMap q_map, const PrefillParams p) {
-  using Shape = PrefillShape<D>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  using Shape = PrefillShape<D, KEYS>;
+  // The swizzled tiles need 1024-byte alignment; the dynamic window is
+  // declared so, and a launch that did not get it reports it and does nothing.
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023u) {
+    if (threadIdx.x == 0) set_error(p.err, kDevErrTimeout);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + Shape::kQBytes;
   uint8_t* sP = sKV + kPfStages * Shape::kStageBytes;
@@ -195,7 +206,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   }
   const int tok_end = min(q_len, tok0 + p.tokens_per_tile);
   const int n_keys = q_start + tok_end;  // keys 0 .. last position of the tile
-  const int n_key_tiles = (n_keys + kPfKeys - 1) / kPfKeys;
+  const int n_key_tiles = (n_keys + KEYS - 1) / KEYS;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -214,7 +225,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (warp == 5) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
+                 "r"(Shape::kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -231,7 +242,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_arrive_expect_tx(q_full, Shape::kQBytes);
 #pragma unroll
       for (int c = 0; c < Shape::kChunks; ++c) {
-        tma_load_3d(sQ + c * kChunkBytes, &q_map, q_full, c * 64, kvh * p.G, row0 + tok0);
+        tma_load_3d(sQ + c * kRegion, &q_map, q_full, c * 64, kvh * p.G, row0 + tok0);
       }
       const int32_t* table = p.block_tables + static_cast<size_t>(seq) * p.max_blocks;
       const int n_pages = (n_keys + 15) >> 4;
@@ -244,10 +255,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           *abort_flag = 1;
           break;
         }
-        int blk[8];
+        int blk[Shape::kPages];
 #pragma unroll
-        for (int pg = 0; pg < 8; ++pg) {
-          const int page = j * 8 + pg;
+        for (int pg = 0; pg < Shape::kPages; ++pg) {
+          const int page = j * Shape::kPages + pg;
           int b = -1;
           if (page < n_pages) {
             if (page < p.max_blocks) {
@@ -266,15 +277,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         uint8_t* sK = sKV + st * Shape::kStageBytes;
         uint8_t* sV = sK + Shape::kKBytes;
 #pragma unroll
-        for (int pg = 0; pg < 8; ++pg) {
+        for (int pg = 0; pg < Shape::kPages; ++pg) {
           const int ck = blk[pg] < 0 ? oob : 2 * blk[pg];
           const int cv = blk[pg] < 0 ? oob : 2 * blk[pg] + 1;
 #pragma unroll
           for (int c = 0; c < Shape::kChunks; ++c) {
-            tma_load_4d(sK + c * kChunkBytes + pg * 16 * 128, &kv_map, kv_full + st, c * 64, 0,
-                        kvh, ck);
-            tma_load_4d(sV + c * kChunkBytes + pg * 16 * 128, &kv_map, kv_full + st, c * 64, 0,
-                        kvh, cv);
+            tma_load_4d(sK + c * Shape::kKRegion + pg * 16 * 128, &kv_map, kv_full + st, c * 64,
+                        0, kvh, ck);
+            tma_load_4d(sV + c * Shape::kKRegion + pg * 16 * 128, &kv_map, kv_full + st, c * 64,
+                        0, kvh, cv);
           }
         }
         issued = j + 1;
@@ -291,8 +302,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // ── MMA issue ─────────────────────────────────────────────────────────────
     if (lane == 0) {
       const uint32_t t_s = tmem_base;
-      const uint32_t t_o = tmem_base + kPfKeys;
-      const uint32_t idesc_qk = f16_idesc<T>(kPfKeys, false);
+      const uint32_t t_o = tmem_base + KEYS;
+      const uint32_t idesc_qk = f16_idesc<T>(KEYS, false);
       const uint32_t idesc_pv = f16_idesc<T>(D, true);
       const uint32_t q_addr = smem_u32(sQ);
       const uint32_t p_addr = smem_u32(sP);
@@ -308,9 +319,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           const int st = (j - 1) % kPfStages;
           const uint32_t v_addr = smem_u32(sKV + st * Shape::kStageBytes + Shape::kKBytes);
 #pragma unroll
-          for (int k = 0; k < kPfKeys / 16; ++k) {
-            const uint64_t a = sw128_desc(p_addr + (k >> 2) * kChunkBytes + (k & 3) * 32, 16, 1024);
-            const uint64_t b = sw128_desc(v_addr + k * 2048, kChunkBytes, 1024);
+          for (int k = 0; k < KEYS / 16; ++k) {
+            const uint64_t a = sw128_desc(p_addr + (k >> 2) * kRegion + (k & 3) * 32, 16, 1024);
+            const uint64_t b = sw128_desc(v_addr + k * 2048, Shape::kKRegion, 1024);
             tc_mma(t_o, a, b, idesc_pv, (j > 1 || k > 0) ? 1u : 0u);
           }
           tc_commit(kv_empty + st);
@@ -326,8 +337,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           const uint32_t k_addr = smem_u32(sKV + st * Shape::kStageBytes);
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
-            const uint64_t a = sw128_desc(q_addr + (k >> 2) * kChunkBytes + (k & 3) * 32, 16, 1024);
-            const uint64_t b = sw128_desc(k_addr + (k >> 2) * kChunkBytes + (k & 3) * 32, 16, 1024);
+            const uint64_t a = sw128_desc(q_addr + (k >> 2) * kRegion + (k & 3) * 32, 16, 1024);
+            const uint64_t b =
+                sw128_desc(k_addr + (k >> 2) * Shape::kKRegion + (k & 3) * 32, 16, 1024);
             tc_mma(t_s, a, b, idesc_qk, k > 0 ? 1u : 0u);
           }
           tc_commit(s_full);
@@ -341,10 +353,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
   } else {
     // ── softmax and epilogue: one row per thread ─────────────────────────────
+    // Two passes over the row of S in TMEM (max, then exp2 and the P store),
+    // 64 columns at a time, so few registers are live.
+    constexpr int kHalves = KEYS / 64;
     const int m = threadIdx.x;  // row = TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
     const uint32_t t_s = tmem_base + lane_base;
-    const uint32_t t_o = tmem_base + lane_base + kPfKeys;
+    const uint32_t t_o = tmem_base + lane_base + KEYS;
     const int t = m >> p.g_shift;
     const int row_pos = q_start + tok0 + t;
     float m_run = -INFINITY;
@@ -357,24 +372,26 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       ok = __all_sync(0xffffffffu, ok) && !aborted(abort_flag);
       if (!ok) break;
       tc_fence_after();
-      uint32_t s[kPfKeys / 16][16];
-#pragma unroll
-      for (int c = 0; c < kPfKeys / 16; ++c) tmem_ld16(t_s + c * 16, s[c]);
-      tmem_ld_wait();
-#pragma unroll
-      for (int c = 0; c < kPfKeys / 16; ++c) tmem_ld_fence_regs(s[c]);
-
-      const int key0 = j * kPfKeys;
-      const bool needs_mask = key0 + kPfKeys - 1 > row_pos;
+      const int key0 = j * KEYS;
+      const bool needs_mask = key0 + KEYS - 1 > row_pos;
+      uint32_t s[4][16];
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kPfKeys / 16; ++c) {
+      for (int h = 0; h < kHalves; ++h) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float x = __uint_as_float(s[c][i]) * p.scale_log2;
-          if (needs_mask && key0 + c * 16 + i > row_pos) x = -INFINITY;
-          s[c][i] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
+        for (int c = 0; c < 4; ++c) tmem_ld16(t_s + h * 64 + c * 16, s[c]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld_fence_regs(s[c]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float x = __uint_as_float(s[c][i]) * p.scale_log2;
+            if (needs_mask && key0 + h * 64 + c * 16 + i > row_pos) x = -INFINITY;
+            s[c][i] = __float_as_uint(x);
+            mx = fmaxf(mx, x);
+          }
         }
       }
       const float m_new = fmaxf(m_run, mx);
@@ -397,26 +414,44 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         l_run *= alpha;
         m_run = m_new;
       }
-      // P = exp2(s - m_run) as 16-bit values into the swizzled K-major P tile.
+      // P = exp2(s - m_run) as 16-bit values into the swizzled K-major P tile
+      // (one 128-byte row per 64 keys; 16-byte chunk index XOR row % 8).
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < kPfKeys / 16; ++c) {
-        uint32_t packed[8];
+      for (int h = 0; h < kHalves; ++h) {
+        if (kHalves > 1) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float a = fast_exp2(__uint_as_float(s[c][2 * i]) - m_run);
-          const float b = fast_exp2(__uint_as_float(s[c][2 * i + 1]) - m_run);
-          sum += a + b;
-          packed[i] = Elt<T>::pack(a, b);
+          for (int c = 0; c < 4; ++c) tmem_ld16(t_s + h * 64 + c * 16, s[c]);
+          tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tmem_ld_fence_regs(s[c]);
         }
-        // 16 keys = two 16-byte chunks of the 128-byte row of this 64-key region.
-        const int region = (c * 16) >> 6;
-        const uint32_t chunk0 = static_cast<uint32_t>(((c * 16) & 63) >> 3);
-        uint8_t* base = p_row + region * kChunkBytes;
-        *reinterpret_cast<uint4*>(base + ((chunk0 ^ sw) << 4)) =
-            make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        *reinterpret_cast<uint4*>(base + (((chunk0 + 1) ^ sw) << 4)) =
-            make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        uint8_t* base = p_row + h * kRegion;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t packed[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float a, b;
+            if (kHalves > 1) {
+              const int k0 = key0 + h * 64 + c * 16 + 2 * i;
+              const bool ma = needs_mask && k0 > row_pos;
+              const bool mb = needs_mask && k0 + 1 > row_pos;
+              a = ma ? 0.f : fast_exp2(__uint_as_float(s[c][2 * i]) * p.scale_log2 - m_run);
+              b = mb ? 0.f : fast_exp2(__uint_as_float(s[c][2 * i + 1]) * p.scale_log2 - m_run);
+            } else {
+              a = fast_exp2(__uint_as_float(s[c][2 * i]) - m_run);
+              b = fast_exp2(__uint_as_float(s[c][2 * i + 1]) - m_run);
+            }
+            sum += a + b;
+            packed[i] = Elt<T>::pack(a, b);
+          }
+          const uint32_t chunk0 = static_cast<uint32_t>(2 * c);
+          *reinterpret_cast<uint4*>(base + ((chunk0 ^ sw) << 4)) =
+              make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          *reinterpret_cast<uint4*>(base + (((chunk0 + 1) ^ sw) << 4)) =
+              make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        }
       }
       l_run += sum;
       fence_proxy_async_smem();
@@ -461,7 +496,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (warp == 5) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(kTmemCols)
+                 "r"(Shape::kTmemCols)
                  : "memory");
   }
 }
@@ -469,16 +504,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 template <typename T, int D>
 int launch_prefill(const CUtensorMap& kv_map, const CUtensorMap& q_map, const PrefillParams& p,
                    dim3 grid, cudaStream_t s) {
-  using Shape = PrefillShape<D>;
+  constexpr int KEYS = D == 64 ? 128 : 64;
+  using Shape = PrefillShape<D, KEYS>;
   static std::once_flag flags[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return fail(VMPS_ERR_CUDA, "device index %d", dev);
   std::call_once(flags[dev], [] {
-    cudaFuncSetAttribute(paged_prefill_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         Shape::kSmemBytes);
+    cudaFuncSetAttribute(paged_prefill_kernel<T, D, KEYS>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmemBytes);
   });
-  paged_prefill_kernel<T, D><<<grid, kPfThreads, Shape::kSmemBytes, s>>>(kv_map, q_map, p);
+  paged_prefill_kernel<T, D, KEYS><<<grid, kPfThreads, Shape::kSmemBytes, s>>>(kv_map, q_map, p);
   return check_launch("paged_prefill_attention");
 }
 
