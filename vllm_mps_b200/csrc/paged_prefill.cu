@@ -11,23 +11,25 @@
 // Work split.  A CTA owns one 128-row tile of one kv head of one sequence.
 // The rows are (query token, query head) pairs: 128/G consecutive tokens x
 // the G query heads that share the kv head, so every K/V tile loaded serves
-// all G heads (GQA is never materialised).  Key tiles are 128 keys (8 pages)
-// for head_dim 64 and 64 keys for head_dim 128.
+// all G heads (GQA is never materialised).  Key tiles are 64 keys (4 pages).
 //
 // Data movement.  Warp 4 (one lane) loads the Q tile with a 3-D TMA and the
 // K and V pages with 4-D TMAs (no multicast), all with the 128-byte swizzle,
-// into a 2-stage ring guarded by mbarriers.  Pages past the sequence's table
-// are fetched at an out-of-range coordinate, which the TMA fills with zeros.
+// into a K ring and a V ring of two tiles each, so K(j+2) loads as soon as
+// QK(j) is done and V(j+2) as soon as PV(j) is.  Pages past the sequence's
+// table are fetched at an out-of-range coordinate (the TMA fills zeros).
 //
 // Math.  Warp 5 (one lane) issues tcgen05.mma (kind::f16, M=128, fp32
-// accumulate): S = Q K^T into KEYS TMEM columns, then O += P V into D more
-// columns, P read from shared memory (K-major) and V as an MN-major operand,
-// so V needs no transpose.  Warps 0-3 own one row each (TMEM lane = row):
-// they read the row of S twice (max, then exp2), apply the causal mask and
-// the scale, keep the
-// running max and sum in fp32 (rescaling O in TMEM only when the max grows
-// by more than 2^8, so most tiles skip it), write P = exp2(s - max) as 16-bit
-// values into the swizzled P tile, and finally normalise O and store it.
+// accumulate).  S(j) = Q K(j)^T goes to one of two 64-column TMEM buffers,
+// so QK(j+1) runs while the softmax works on S(j).  The softmax warps write
+// P(j) as 16-bit pairs over the first 32 columns of S(j)'s own buffer and
+// PV(j) reads it from there as a TMEM A operand (V as an MN-major shared-
+// memory operand, no transpose), accumulating O in 128 more columns.  Warps
+// 0-3 own one row each (TMEM lane = row): mask by position, running max and
+// sum in fp32 with exp2; O is rescaled in TMEM only when a row's max grows by
+// more than 2^8 (then after PV(j-1) has landed), so most tiles never wait on
+// the previous PV.  Two CTAs share each SM (~96 KB of shared memory, 256
+// TMEM columns each).
 //
 // Safety.  Every mbarrier wait is bounded; a wait that gives up sets
 // kDevErrTimeout and a CTA-wide abort flag, all roles leave their loops,
@@ -43,26 +45,23 @@ namespace vmps {
 namespace {
 
 constexpr int kPfRows = 128;       // MMA M: rows per tile
-constexpr int kPfStages = 2;       // K/V ring depth
+constexpr int kPfKeys = 64;        // keys per key tile (4 pages)
+constexpr int kPfPages = kPfKeys / 16;
+constexpr int kPfStages = 2;       // K ring and V ring depth
 constexpr int kPfThreads = 192;    // warps 0-3 softmax, 4 loads, 5 MMA
 constexpr int kRegion = 128 * 128; // 128 rows x 64 16-bit columns (one swizzle span)
+constexpr int kKRegion = kPfKeys * 128;  // one 64-column chunk of a key tile
 
-// KEYS = keys per key tile: 128 for head_dim 64, 64 for head_dim 128, so
-// that a CTA needs ~113 KB of shared memory and two CTAs share an SM (one's
-// softmax runs while the other's MMAs do).
-template <int D, int KEYS>
+template <int D>
 struct PrefillShape {
   static constexpr int kChunks = D / 64;
-  static constexpr int kPages = KEYS / 16;
   static constexpr int kQBytes = kChunks * kRegion;
-  static constexpr int kKRegion = KEYS * 128;             // one 64-column chunk of a key tile
-  static constexpr int kKBytes = kChunks * kKRegion;      // K (or V) of one key tile
-  static constexpr int kStageBytes = 2 * kKBytes;
-  static constexpr int kPBytes = (KEYS / 64) * kRegion;
-  static constexpr int kBarBytes = 128;
-  static constexpr int kSmemBytes = kQBytes + kPfStages * kStageBytes + kPBytes + kBarBytes;
-  // TMEM: S in columns [0, KEYS), O in [KEYS, KEYS + D); power of two >= 32.
-  static constexpr uint32_t kTmemCols = (KEYS + D <= 128) ? 128u : 256u;
+  static constexpr int kTileBytes = kChunks * kKRegion;  // K (or V) of one key tile
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemBytes = kQBytes + 2 * kPfStages * kTileBytes + kBarBytes;
+  // TMEM: S double buffer in columns [0, 2 KEYS) (P(j) overwrites the first
+  // KEYS/2 columns of S(j)), O in [2 KEYS, 2 KEYS + D).
+  static constexpr uint32_t kTmemCols = 256;
 };
 
 struct PrefillParams {
@@ -104,6 +103,20 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
       : "memory");
 }
 
+// Same with A read from TMEM (K-major: row = lane, 16-bit pairs along K per
+// 32-bit column, 8 columns per K-step of 16).
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // 16 consecutive 32-bit TMEM columns of this thread's lane.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -137,10 +150,6 @@ __device__ __forceinline__ void tmem_ld_fence_regs(uint32_t (&r)[16]) {
   for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(r[i]));
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand
 // (sm_100 format: start, leading and stride byte offsets in 16-byte units,
 // descriptor version 1 at bit 46, layout type 2 = SWIZZLE_128B at bit 61).
@@ -163,11 +172,12 @@ __device__ __forceinline__ uint32_t f16_idesc(int n, bool b_mn_major) {
 
 __device__ __forceinline__ bool aborted(volatile int* flag) { return *flag != 0; }
 
-template <typename T, int D, int KEYS>
+template <typename T, int D>
 __global__ void __launch_bounds__(kPfThreads, 2)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap kv_map,
                          const __grid_constant__ CUtensorMap q_map, const PrefillParams p) {
-  using Shape = PrefillShape<D, KEYS>;
+  using Shape = PrefillShape<D>;
+  constexpr int KEYS = kPfKeys;
   // The swizzled tiles need 1024-byte alignment; the dynamic window is
   // declared so, and a launch that did not get it reports it and does nothing.
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -175,18 +185,20 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     if (threadIdx.x == 0) set_error(p.err, kDevErrTimeout);
     return;
   }
-  uint8_t* smem = smem_raw;
-  uint8_t* sQ = smem;
-  uint8_t* sKV = sQ + Shape::kQBytes;
-  uint8_t* sP = sKV + kPfStages * Shape::kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + Shape::kPBytes);
+  uint8_t* sQ = smem_raw;
+  uint8_t* sK = sQ + Shape::kQBytes;                 // K ring: kPfStages tiles
+  uint8_t* sV = sK + kPfStages * Shape::kTileBytes;  // V ring: kPfStages tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kPfStages * Shape::kTileBytes);
   uint64_t* q_full = bars + 0;
-  uint64_t* s_full = bars + 1;
-  uint64_t* p_full = bars + 2;
-  uint64_t* o_done = bars + 3;
-  uint64_t* kv_full = bars + 4;
-  uint64_t* kv_empty = bars + 4 + kPfStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 + 2 * kPfStages);
+  uint64_t* p_full = bars + 1;   // softmax -> MMA: P(j) in TMEM, O rescaled
+  uint64_t* o_ready = bars + 2;  // MMA -> softmax: PV(j) complete
+  uint64_t* o_done = bars + 3;   // all MMAs complete
+  uint64_t* s_full = bars + 4;   // [2]: S(j) in TMEM buffer j % 2
+  uint64_t* k_full = bars + 6;   // [kPfStages]
+  uint64_t* k_empty = k_full + kPfStages;
+  uint64_t* v_full = k_empty + kPfStages;
+  uint64_t* v_empty = v_full + kPfStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_empty + kPfStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int seq = blockIdx.z;
@@ -212,12 +224,16 @@ __global__ void __launch_bounds__(kPfThreads, 2)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(s_full, 1);
     mbar_init(p_full, 4);
+    mbar_init(o_ready, 1);
     mbar_init(o_done, 1);
+    mbar_init(s_full + 0, 1);
+    mbar_init(s_full + 1, 1);
     for (int s = 0; s < kPfStages; ++s) {
-      mbar_init(kv_full + s, 1);
-      mbar_init(kv_empty + s, 1);
+      mbar_init(k_full + s, 1);
+      mbar_init(k_empty + s, 1);
+      mbar_init(v_full + s, 1);
+      mbar_init(v_empty + s, 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -235,7 +251,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 4) {
-    // ── loads ────────────────────────────────────────────────────────────────
+    // ── loads: Q once, then K(j) and V(j) into their own rings ───────────────
     if (lane == 0) {
       prefetch_tmap(&q_map);
       prefetch_tmap(&kv_map);
@@ -247,18 +263,14 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       const int32_t* table = p.block_tables + static_cast<size_t>(seq) * p.max_blocks;
       const int n_pages = (n_keys + 15) >> 4;
       const int oob = 2 * p.num_blocks;  // past the pool: the TMA fills zeros
-      int issued = 0;
+      int k_issued = 0, v_issued = 0;
       for (int j = 0; j < n_key_tiles; ++j) {
         const int st = j % kPfStages;
-        if (j >= kPfStages &&
-            (!mbar_wait(kv_empty + st, ((j / kPfStages) - 1) & 1, p.err) || aborted(abort_flag))) {
-          *abort_flag = 1;
-          break;
-        }
-        int blk[Shape::kPages];
+        const uint32_t ph = ((j / kPfStages) - 1) & 1;
+        int blk[kPfPages];
 #pragma unroll
-        for (int pg = 0; pg < Shape::kPages; ++pg) {
-          const int page = j * Shape::kPages + pg;
+        for (int pg = 0; pg < kPfPages; ++pg) {
+          const int page = j * kPfPages + pg;
           int b = -1;
           if (page < n_pages) {
             if (page < p.max_blocks) {
@@ -273,77 +285,101 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           }
           blk[pg] = b;
         }
-        mbar_arrive_expect_tx(kv_full + st, Shape::kStageBytes);
-        uint8_t* sK = sKV + st * Shape::kStageBytes;
-        uint8_t* sV = sK + Shape::kKBytes;
+        // K(j) once QK(j - stages) is done with the slot.
+        if (j >= kPfStages && (!mbar_wait(k_empty + st, ph, p.err) || aborted(abort_flag))) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(k_full + st, Shape::kTileBytes);
 #pragma unroll
-        for (int pg = 0; pg < Shape::kPages; ++pg) {
+        for (int pg = 0; pg < kPfPages; ++pg) {
           const int ck = blk[pg] < 0 ? oob : 2 * blk[pg];
+#pragma unroll
+          for (int c = 0; c < Shape::kChunks; ++c) {
+            tma_load_4d(sK + st * Shape::kTileBytes + c * kKRegion + pg * 2048, &kv_map,
+                        k_full + st, c * 64, 0, kvh, ck);
+          }
+        }
+        k_issued = j + 1;
+        // V(j) once PV(j - stages) is done with the slot.
+        if (j >= kPfStages && (!mbar_wait(v_empty + st, ph, p.err) || aborted(abort_flag))) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(v_full + st, Shape::kTileBytes);
+#pragma unroll
+        for (int pg = 0; pg < kPfPages; ++pg) {
           const int cv = blk[pg] < 0 ? oob : 2 * blk[pg] + 1;
 #pragma unroll
           for (int c = 0; c < Shape::kChunks; ++c) {
-            tma_load_4d(sK + c * Shape::kKRegion + pg * 16 * 128, &kv_map, kv_full + st, c * 64,
-                        0, kvh, ck);
-            tma_load_4d(sV + c * Shape::kKRegion + pg * 16 * 128, &kv_map, kv_full + st, c * 64,
-                        0, kvh, cv);
+            tma_load_4d(sV + st * Shape::kTileBytes + c * kKRegion + pg * 2048, &kv_map,
+                        v_full + st, c * 64, 0, kvh, cv);
           }
         }
-        issued = j + 1;
+        v_issued = j + 1;
       }
       if (aborted(abort_flag)) {
         // Let this CTA's own loads land before its shared memory is released.
         mbar_wait(q_full, 0, p.err);
-        for (int j = max(0, issued - kPfStages); j < issued; ++j) {
-          mbar_wait(kv_full + (j % kPfStages), (j / kPfStages) & 1, p.err);
+        for (int j = max(0, k_issued - kPfStages); j < k_issued; ++j) {
+          mbar_wait(k_full + (j % kPfStages), (j / kPfStages) & 1, p.err);
+        }
+        for (int j = max(0, v_issued - kPfStages); j < v_issued; ++j) {
+          mbar_wait(v_full + (j % kPfStages), (j / kPfStages) & 1, p.err);
         }
       }
     }
   } else if (warp == 5) {
     // ── MMA issue ─────────────────────────────────────────────────────────────
+    // Order: QK(0), QK(1), then per tile j: PV(j) [after the softmax of j],
+    // QK(j + 2) into the S buffer PV(j) just read P from (MMAs of one thread
+    // execute in issue order).
     if (lane == 0) {
-      const uint32_t t_s = tmem_base;
-      const uint32_t t_o = tmem_base + KEYS;
+      const uint32_t t_o = tmem_base + 2 * KEYS;
       const uint32_t idesc_qk = f16_idesc<T>(KEYS, false);
       const uint32_t idesc_pv = f16_idesc<T>(D, true);
       const uint32_t q_addr = smem_u32(sQ);
-      const uint32_t p_addr = smem_u32(sP);
-      bool ok = mbar_wait(q_full, 0, p.err);
-      for (int j = 0; ok && j <= n_key_tiles; ++j) {
-        if (j > 0) {
-          // O += P(j-1) V(j-1)
-          if (!mbar_wait(p_full, (j - 1) & 1, p.err) || aborted(abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const int st = (j - 1) % kPfStages;
-          const uint32_t v_addr = smem_u32(sKV + st * Shape::kStageBytes + Shape::kKBytes);
+      bool ok = mbar_wait(q_full, 0, p.err) && !aborted(abort_flag);
+      auto issue_qk = [&](int j) -> bool {
+        const int st = j % kPfStages;
+        if (!mbar_wait(k_full + st, (j / kPfStages) & 1, p.err) || aborted(abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sK + st * Shape::kTileBytes);
+        const uint32_t t_s = tmem_base + (j & 1) * KEYS;
 #pragma unroll
-          for (int k = 0; k < KEYS / 16; ++k) {
-            const uint64_t a = sw128_desc(p_addr + (k >> 2) * kRegion + (k & 3) * 32, 16, 1024);
-            const uint64_t b = sw128_desc(v_addr + k * 2048, Shape::kKRegion, 1024);
-            tc_mma(t_o, a, b, idesc_pv, (j > 1 || k > 0) ? 1u : 0u);
-          }
-          tc_commit(kv_empty + st);
+        for (int k = 0; k < D / 16; ++k) {
+          const uint64_t a = sw128_desc(q_addr + (k >> 2) * kRegion + (k & 3) * 32, 16, 1024);
+          const uint64_t b = sw128_desc(k_addr + (k >> 2) * kKRegion + (k & 3) * 32, 16, 1024);
+          tc_mma(t_s, a, b, idesc_qk, k > 0 ? 1u : 0u);
         }
-        if (j < n_key_tiles) {
-          // S = Q K(j)^T
-          const int st = j % kPfStages;
-          if (!mbar_wait(kv_full + st, (j / kPfStages) & 1, p.err) || aborted(abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sKV + st * Shape::kStageBytes);
+        tc_commit(k_empty + st);
+        tc_commit(s_full + (j & 1));
+        return true;
+      };
+      if (ok) ok = issue_qk(0);
+      if (ok && n_key_tiles > 1) ok = issue_qk(1);
+      for (int j = 0; ok && j < n_key_tiles; ++j) {
+        // O += P(j) V(j), P(j) read from TMEM where S(j) was.
+        if (!mbar_wait(p_full, j & 1, p.err) || aborted(abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int st = j % kPfStages;
+        if (!mbar_wait(v_full + st, (j / kPfStages) & 1, p.err) || aborted(abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + st * Shape::kTileBytes);
+        const uint32_t t_p = tmem_base + (j & 1) * KEYS;
 #pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            const uint64_t a = sw128_desc(q_addr + (k >> 2) * kRegion + (k & 3) * 32, 16, 1024);
-            const uint64_t b =
-                sw128_desc(k_addr + (k >> 2) * Shape::kKRegion + (k & 3) * 32, 16, 1024);
-            tc_mma(t_s, a, b, idesc_qk, k > 0 ? 1u : 0u);
-          }
-          tc_commit(s_full);
+        for (int k = 0; k < KEYS / 16; ++k) {
+          const uint64_t b = sw128_desc(v_addr + k * 2048, kKRegion, 1024);
+          tc_mma_ts(t_o, t_p + k * 8, b, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
         }
+        tc_commit(v_empty + st);
+        tc_commit(o_ready);
+        if (j + 2 < n_key_tiles) ok = issue_qk(j + 2);
       }
       if (!ok) *abort_flag = 1;
       // Whatever happened, every MMA this lane issued completes before the
@@ -353,52 +389,61 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     }
   } else {
     // ── softmax and epilogue: one row per thread ─────────────────────────────
-    // Two passes over the row of S in TMEM (max, then exp2 and the P store),
-    // 64 columns at a time, so few registers are live.
-    constexpr int kHalves = KEYS / 64;
     const int m = threadIdx.x;  // row = TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t t_s = tmem_base + lane_base;
-    const uint32_t t_o = tmem_base + lane_base + KEYS;
+    const uint32_t t_o = tmem_base + lane_base + 2 * KEYS;
     const int t = m >> p.g_shift;
     const int row_pos = q_start + tok0 + t;
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = true;
-    uint8_t* p_row = sP + m * 128;
-    const uint32_t sw = static_cast<uint32_t>(m & 7);
     for (int j = 0; j < n_key_tiles; ++j) {
-      ok = mbar_wait(s_full, j & 1, p.err);
+      ok = mbar_wait(s_full + (j & 1), (j >> 1) & 1, p.err);
       ok = __all_sync(0xffffffffu, ok) && !aborted(abort_flag);
       if (!ok) break;
       tc_fence_after();
+      const uint32_t t_s = tmem_base + lane_base + (j & 1) * KEYS;
+      uint32_t s[KEYS / 16][16];
+#pragma unroll
+      for (int c = 0; c < KEYS / 16; ++c) tmem_ld16(t_s + c * 16, s[c]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < KEYS / 16; ++c) tmem_ld_fence_regs(s[c]);
       const int key0 = j * KEYS;
-      const bool needs_mask = key0 + KEYS - 1 > row_pos;
-      uint32_t s[4][16];
+      // The max is taken on raw scores (the scale is positive) and the scale
+      // is folded into the exp2 argument: p = exp2(s * scale - m).  Masked
+      // keys (position > row) become -inf; the warp takes the masked path
+      // together whenever any of its rows needs it.
+      const bool needs_mask = __any_sync(0xffffffffu, key0 + KEYS - 1 > row_pos);
       float mx = -INFINITY;
+      if (needs_mask) {
 #pragma unroll
-      for (int h = 0; h < kHalves; ++h) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld16(t_s + h * 64 + c * 16, s[c]);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld_fence_regs(s[c]);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < KEYS / 16; ++c) {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            float x = __uint_as_float(s[c][i]) * p.scale_log2;
-            if (needs_mask && key0 + h * 64 + c * 16 + i > row_pos) x = -INFINITY;
-            s[c][i] = __float_as_uint(x);
-            mx = fmaxf(mx, x);
+            if (key0 + c * 16 + i > row_pos) s[c][i] = __float_as_uint(-INFINITY);
+            mx = fmaxf(mx, __uint_as_float(s[c][i]));
           }
         }
+      } else {
+#pragma unroll
+        for (int c = 0; c < KEYS / 16; ++c) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) mx = fmaxf(mx, __uint_as_float(s[c][i]));
+        }
       }
+      mx *= p.scale_log2;
       const float m_new = fmaxf(m_run, mx);
       if (j == 0) {
         m_run = m_new;
       } else if (__any_sync(0xffffffffu, m_new > m_run + 8.f)) {
-        // Rescale this warp's O rows; rows whose max did not grow use 1.
+        // Rescale this warp's O rows once PV(j - 1) has landed; rows whose
+        // max did not grow use 1.  (Only PV(j - 1) can have completed since
+        // the last wait on o_ready, so its parity is unambiguous.)
+        ok = mbar_wait(o_ready, (j - 1) & 1, p.err);
+        ok = __all_sync(0xffffffffu, ok) && !aborted(abort_flag);
+        if (!ok) break;
+        tc_fence_after();
         const float alpha = fast_exp2(m_run - m_new);
 #pragma unroll
         for (int c = 0; c < D / 16; ++c) {
@@ -410,51 +455,29 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
           tmem_st16(t_o + c * 16, o);
         }
-        tmem_st_wait();
         l_run *= alpha;
         m_run = m_new;
       }
-      // P = exp2(s - m_run) as 16-bit values into the swizzled K-major P tile
-      // (one 128-byte row per 64 keys; 16-byte chunk index XOR row % 8).
+      // P = exp2(s - m_run) as 16-bit pairs over the first KEYS/2 columns of
+      // this S buffer (A operand of PV(j) in TMEM: row = lane, key pairs per
+      // 32-bit column).
       float sum = 0.f;
+      uint32_t pk[KEYS / 32][16];
 #pragma unroll
-      for (int h = 0; h < kHalves; ++h) {
-        if (kHalves > 1) {
+      for (int c = 0; c < KEYS / 16; ++c) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) tmem_ld16(t_s + h * 64 + c * 16, s[c]);
-          tmem_ld_wait();
-#pragma unroll
-          for (int c = 0; c < 4; ++c) tmem_ld_fence_regs(s[c]);
-        }
-        uint8_t* base = p_row + h * kRegion;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t packed[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float a, b;
-            if (kHalves > 1) {
-              const int k0 = key0 + h * 64 + c * 16 + 2 * i;
-              const bool ma = needs_mask && k0 > row_pos;
-              const bool mb = needs_mask && k0 + 1 > row_pos;
-              a = ma ? 0.f : fast_exp2(__uint_as_float(s[c][2 * i]) * p.scale_log2 - m_run);
-              b = mb ? 0.f : fast_exp2(__uint_as_float(s[c][2 * i + 1]) * p.scale_log2 - m_run);
-            } else {
-              a = fast_exp2(__uint_as_float(s[c][2 * i]) - m_run);
-              b = fast_exp2(__uint_as_float(s[c][2 * i + 1]) - m_run);
-            }
-            sum += a + b;
-            packed[i] = Elt<T>::pack(a, b);
-          }
-          const uint32_t chunk0 = static_cast<uint32_t>(2 * c);
-          *reinterpret_cast<uint4*>(base + ((chunk0 ^ sw) << 4)) =
-              make_uint4(packed[0], packed[1], packed[2], packed[3]);
-          *reinterpret_cast<uint4*>(base + (((chunk0 + 1) ^ sw) << 4)) =
-              make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        for (int i = 0; i < 8; ++i) {
+          const float a = fast_exp2(fmaf(__uint_as_float(s[c][2 * i]), p.scale_log2, -m_run));
+          const float b =
+              fast_exp2(fmaf(__uint_as_float(s[c][2 * i + 1]), p.scale_log2, -m_run));
+          sum += a + b;
+          pk[c >> 1][(c & 1) * 8 + i] = Elt<T>::pack(a, b);
         }
       }
+#pragma unroll
+      for (int c = 0; c < KEYS / 32; ++c) tmem_st16(t_s + c * 16, pk[c]);
+      tmem_st_wait();
       l_run += sum;
-      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
@@ -504,17 +527,16 @@ __global__ void __launch_bounds__(kPfThreads, 2)
 template <typename T, int D>
 int launch_prefill(const CUtensorMap& kv_map, const CUtensorMap& q_map, const PrefillParams& p,
                    dim3 grid, cudaStream_t s) {
-  constexpr int KEYS = D == 64 ? 128 : 64;
-  using Shape = PrefillShape<D, KEYS>;
+  using Shape = PrefillShape<D>;
   static std::once_flag flags[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return fail(VMPS_ERR_CUDA, "device index %d", dev);
   std::call_once(flags[dev], [] {
-    cudaFuncSetAttribute(paged_prefill_kernel<T, D, KEYS>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmemBytes);
+    cudaFuncSetAttribute(paged_prefill_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Shape::kSmemBytes);
   });
-  paged_prefill_kernel<T, D, KEYS><<<grid, kPfThreads, Shape::kSmemBytes, s>>>(kv_map, q_map, p);
+  paged_prefill_kernel<T, D><<<grid, kPfThreads, Shape::kSmemBytes, s>>>(kv_map, q_map, p);
   return check_launch("paged_prefill_attention");
 }
 
