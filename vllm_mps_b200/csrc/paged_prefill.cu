@@ -415,23 +415,25 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       // keys (position > row) become -inf; the warp takes the masked path
       // together whenever any of its rows needs it.
       const bool needs_mask = __any_sync(0xffffffffu, key0 + KEYS - 1 > row_pos);
-      float mx = -INFINITY;
+      // Four independent partial maxima (short dependency chains).
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if (needs_mask) {
 #pragma unroll
         for (int c = 0; c < KEYS / 16; ++c) {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             if (key0 + c * 16 + i > row_pos) s[c][i] = __float_as_uint(-INFINITY);
-            mx = fmaxf(mx, __uint_as_float(s[c][i]));
+            mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(s[c][i]));
           }
         }
       } else {
 #pragma unroll
         for (int c = 0; c < KEYS / 16; ++c) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) mx = fmaxf(mx, __uint_as_float(s[c][i]));
+          for (int i = 0; i < 16; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(s[c][i]));
         }
       }
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       mx *= p.scale_log2;
       const float m_new = fmaxf(m_run, mx);
       if (j == 0) {
@@ -461,7 +463,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       // P = exp2(s - m_run) as 16-bit pairs over the first KEYS/2 columns of
       // this S buffer (A operand of PV(j) in TMEM: row = lane, key pairs per
       // 32-bit column).
-      float sum = 0.f;
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent partial sums
       uint32_t pk[KEYS / 32][16];
 #pragma unroll
       for (int c = 0; c < KEYS / 16; ++c) {
@@ -470,10 +472,11 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           const float a = fast_exp2(fmaf(__uint_as_float(s[c][2 * i]), p.scale_log2, -m_run));
           const float b =
               fast_exp2(fmaf(__uint_as_float(s[c][2 * i + 1]), p.scale_log2, -m_run));
-          sum += a + b;
+          sum4[i & 3] += a + b;
           pk[c >> 1][(c & 1) * 8 + i] = Elt<T>::pack(a, b);
         }
       }
+      const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
 #pragma unroll
       for (int c = 0; c < KEYS / 32; ++c) tmem_st16(t_s + c * 16, pk[c]);
       tmem_st_wait();
