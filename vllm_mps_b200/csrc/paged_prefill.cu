@@ -190,11 +190,15 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   uint8_t* sV = sK + kPfStages * Shape::kTileBytes;  // V ring: kPfStages tiles
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kPfStages * Shape::kTileBytes);
   uint64_t* q_full = bars + 0;
-  uint64_t* p_full = bars + 1;   // softmax -> MMA: P(j) in TMEM, O rescaled
-  uint64_t* o_ready = bars + 2;  // MMA -> softmax: PV(j) complete
-  uint64_t* o_done = bars + 3;   // all MMAs complete
-  uint64_t* s_full = bars + 4;   // [2]: S(j) in TMEM buffer j % 2
-  uint64_t* k_full = bars + 6;   // [kPfStages]
+  uint64_t* o_ready = bars + 1;  // MMA -> softmax: PV(j) complete
+  uint64_t* o_done = bars + 2;   // all MMAs complete
+  uint64_t* s_full = bars + 3;   // [2]: S(j) in TMEM buffer j % 2
+  // [2]: softmax -> MMA, P(j) in TMEM buffer j % 2 and O rescaled.  One per
+  // buffer: a softmax warp may finish tile j + 1 (S(j + 1) is computed ahead)
+  // before another warp finishes tile j, and its arrival must not count
+  // toward tile j.
+  uint64_t* p_full = bars + 5;
+  uint64_t* k_full = bars + 7;   // [kPfStages]
   uint64_t* k_empty = k_full + kPfStages;
   uint64_t* v_full = k_empty + kPfStages;
   uint64_t* v_empty = v_full + kPfStages;
@@ -224,7 +228,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(p_full, 4);
+    mbar_init(p_full + 0, 4);
+    mbar_init(p_full + 1, 4);
     mbar_init(o_ready, 1);
     mbar_init(o_done, 1);
     mbar_init(s_full + 0, 1);
@@ -360,7 +365,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       if (ok && n_key_tiles > 1) ok = issue_qk(1);
       for (int j = 0; ok && j < n_key_tiles; ++j) {
         // O += P(j) V(j), P(j) read from TMEM where S(j) was.
-        if (!mbar_wait(p_full, j & 1, p.err) || aborted(abort_flag)) {
+        if (!mbar_wait(p_full + (j & 1), (j >> 1) & 1, p.err) || aborted(abort_flag)) {
           ok = false;
           break;
         }
@@ -483,7 +488,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       l_run += sum;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(p_full + (j & 1));
     }
     // Epilogue: O / l for rows of this sequence.
     bool done = ok && mbar_wait(o_done, 0, p.err);
