@@ -49,3 +49,23 @@ def cuda_device():
     if not torch.cuda.is_available():
         pytest.fail("this test needs a CUDA device")
     return torch.device("cuda", 0)
+
+
+@pytest.fixture(autouse=True)
+def device_error_word_stays_clear(request):
+    """After every GPU test the kernels' device error word must be clear.
+
+    Tests that provoke an error on purpose read (and so clear) the word
+    themselves; any other bit left set means a kernel skipped an access.
+    """
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    import torch
+
+    if not torch.cuda.is_available():
+        return
+    from vllm_mps_b200 import kernels as K
+
+    word = K.error_word(torch.device("cuda", 0))
+    assert word == 0, f"device error word {word} left set by {request.node.name}"

@@ -157,6 +157,16 @@ class LLMEngine:
         seqs = [s for g in sched_out.scheduled_groups for s in g.get_seqs(SequenceStatus.RUNNING)]
         if not seqs:
             return []
+        # A sequence resumed from preemption gets its old slots back but no
+        # slot for the token it processes now: the reference scheduler appends
+        # only for groups that were already running (engine/scheduler.py:98-125,
+        # 189-196), and its engine then writes that token past the block
+        # table's count (an IndexError at a page boundary, mps_memory_pool.py:257-268).
+        # Give every scheduled sequence a slot for each of its tokens.
+        kv = self.kv_cache_manager
+        for s in seqs:
+            while kv._block_tables[s.seq_id].num_tokens() < s.get_total_len():
+                kv.append_slot(s.seq_id)
         if self.mode == "physical":
             self._prefill([s for s in seqs if s.seq_id not in self._prefilled])
         seq_ids = [s.seq_id for s in seqs]
