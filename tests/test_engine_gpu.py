@@ -80,23 +80,27 @@ def test_c0_greedy_parity_with_reference(c0_model, record_property):
     for p in prompts:
         eng.add_request(p, SamplingParams(temperature=0.0, max_tokens=20))
     recorded = []
-    real_forward = eng.adapter.forward_batch
 
-    def forward(token_ids, seq_ids, positions, seq_lens):
-        t = len(recorded)
-        if t in restarts:
-            blocks, bits = restarts[t]
-            pool = eng.memory_pool.layer(0)
-            src = torch.from_numpy(bits.view(np.int16)).view(torch.float16).to(pool.device)
-            pool[torch.from_numpy(blocks).to(pool.device)] = src
-        return real_forward(token_ids, seq_ids, positions, seq_lens)
+    def with_restarts(real_forward):
+        def forward(token_ids, seq_ids, positions, seq_lens):
+            t = len(recorded)
+            if t in restarts:
+                blocks, bits = restarts[t]
+                pool = eng.memory_pool.layer(0)
+                src = torch.from_numpy(bits.view(np.int16)).view(torch.float16).to(pool.device)
+                pool[torch.from_numpy(blocks).to(pool.device)] = src
+            return real_forward(token_ids, seq_ids, positions, seq_lens)
+        return forward
 
     def forced(logits, params, generator=None):
         recorded.append(logits.float().cpu())
         t = len(recorded) - 1
         return [int(ref_tokens[s][t]) for s in step_seqs[t]]
 
-    eng.adapter.forward_batch = forward
+    # The step runs as a CUDA graph (decode_graph) or eagerly: hook both.
+    eng.adapter.forward_batch = with_restarts(eng.adapter.forward_batch)
+    if eng._graphs is not None:
+        eng._graphs.run = with_restarts(eng._graphs.run)
     eng.sampler.sample_rows = forced
     steps = 0
     while not eng.is_finished():
@@ -261,3 +265,43 @@ def test_single_token_path_matches_batch():
     batch = ad.forward_batch([prompt[-1]], [901], [len(prompt)], [len(prompt) + 1])
     kv.free(901)
     assert (single.float() - batch[0].float()).abs().max().item() < 0.05
+
+
+def test_graph_decode_matches_eager_decode():
+    """The CUDA-graph decode step (batch padded to a bucket) against the eager
+    HF forward: same tokens wherever the margin is not a near tie, logits
+    within 2e-2 (the GEMMs run at the bucket's row count)."""
+    from vllm_mps_b200.core.sequence import SamplingParams
+    from vllm_mps_b200.engine.llm_engine import LLMEngine
+
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(0, 1024, size=n).tolist() for n in (3, 17, 40, 9, 64)]
+    runs = {}
+    for graphs in (True, False):
+        eng = LLMEngine.from_model(_small_llama(seed=4), num_gpu_blocks=64, num_cpu_blocks=8,
+                                   max_batch_size=8, max_tokens_per_step=10000, mode="physical",
+                                   device="cuda", cuda_graphs=graphs)
+        seen = []
+        real = eng.sampler.sample_rows
+
+        def spy(logits, params, generator=None, seen=seen, real=real):
+            seen.append(logits.float().cpu())
+            return real(logits, params, generator)
+
+        eng.sampler.sample_rows = spy
+        for p in prompts:
+            eng.add_request(p, SamplingParams(temperature=0.0, max_tokens=12))
+        while not eng.is_finished():
+            eng.step()
+        runs[graphs] = ([eng.get_output(i).token_ids for i in range(5)], seen)
+        if graphs:
+            assert eng._graphs is not None and eng._graphs._graphs  # a graph was replayed
+    (tg, lg), (te, le) = runs[True], runs[False]
+    for t in range(len(le)):
+        assert (lg[t] - le[t]).abs().max().item() < 2e-2, t
+    for i in range(5):
+        for t, (a, b) in enumerate(zip(tg[i], te[i])):
+            if a != b:
+                top2 = torch.topk(le[t][i], 2).values
+                assert float(top2[0] - top2[1]) < 2e-2, (i, t)
+                break

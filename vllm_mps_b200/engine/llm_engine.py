@@ -17,9 +17,10 @@ Two modes:
   context.  ``swap=True`` also copies preempted blocks to pinned host memory
   and back (the reference's swap moves metadata only).
 
-Per step the decode batch is one HF forward whose attention layers each run
-one fused sm_100a kernel; greedy sampling of the whole batch is one device
-argmax and one host copy.
+Per step the decode batch runs every layer with one fused sm_100a attention
+kernel; on CUDA the step is a CUDA graph captured per batch bucket
+(``engine/decode_graph.py``, ``cuda_graphs=True``), else an eager HF forward.
+Greedy sampling of the whole batch is one device argmax and one host copy.
 """
 
 from __future__ import annotations
@@ -83,7 +84,7 @@ class LLMEngine:
                    swap: bool = False, preempt_watermark: float | None = None,
                    dtype: torch.dtype | None = None,
                    device: torch.device | str | None = None,
-                   max_prefill_rows: int = 8192) -> "LLMEngine":
+                   max_prefill_rows: int = 8192, cuda_graphs: bool = True) -> "LLMEngine":
         from vllm_mps_b200.models.llama_adapter import LlamaAdapter
 
         if mode not in ("compat", "physical"):
@@ -117,6 +118,12 @@ class LLMEngine:
         if max_prefill_rows < 1:
             raise ValueError("max_prefill_rows must be >= 1")
         eng.max_prefill_rows = int(max_prefill_rows)
+        eng._graphs = None
+        if cuda_graphs and cfg.device.type == "cuda":
+            from vllm_mps_b200.engine.decode_graph import DecodeGraphRunner
+
+            max_blocks = (max(cfg.max_seq_len, 1) + BLOCK_SIZE - 1) // BLOCK_SIZE + 1
+            eng._graphs = DecodeGraphRunner(eng.adapter, kv, BLOCK_SIZE, max_blocks)
         eng.total_tokens_generated = 0
         eng.start_time = time.time()
         return eng
@@ -173,7 +180,10 @@ class LLMEngine:
         token_ids = [s.get_last_token_id() for s in seqs]
         positions = [s.get_total_len() - 1 for s in seqs]
         seq_lens = [s.get_total_len() for s in seqs]
-        logits = self.adapter.forward_batch(token_ids, seq_ids, positions, seq_lens)
+        if self._graphs is not None and self._graphs.can_run(seq_ids):
+            logits = self._graphs.run(token_ids, seq_ids, positions, seq_lens)
+        else:
+            logits = self.adapter.forward_batch(token_ids, seq_ids, positions, seq_lens)
         next_tokens = self.sampler.sample_rows(
             logits, [self._seq_to_params.get(sid, SamplingParams()) for sid in seq_ids])
         return self._update_sequences(seq_ids, next_tokens)
