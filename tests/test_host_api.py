@@ -178,6 +178,46 @@ def test_greedy_sampler_takes_first_index_on_ties():
     assert tok[0] in (1, 2) and tok[1] == 0
 
 
+def test_batched_sampling_matches_reference_distribution():
+    """Temperature + top-k + top-p of several rows in one batched pass give
+    each row the distribution of the reference's per-row steps
+    (model/sampler.py:36-59): same support, frequencies within sampling noise."""
+    import torch.nn.functional as F
+
+    from vllm_mps_b200.core.sequence import SamplingParams
+    from vllm_mps_b200.model.sampler import Sampler
+
+    torch.manual_seed(0)
+    logits = torch.randn(4, 50)
+    params = [SamplingParams(temperature=0.7, top_k=5), SamplingParams(temperature=1.3, top_p=0.6),
+              SamplingParams(temperature=1.0, top_k=10, top_p=0.8), SamplingParams(temperature=0.0)]
+
+    def reference_probs(l, p):
+        l = l / p.temperature
+        if p.top_k > 0:
+            th = torch.topk(l, p.top_k).values[-1]
+            l = torch.where(l < th, torch.tensor(float("-inf")), l)
+        if p.top_p < 1.0:
+            sl, si = torch.sort(l, descending=True)
+            pr = F.softmax(sl, -1)
+            sl = sl.masked_fill(torch.cumsum(pr, -1) - pr >= p.top_p, float("-inf"))
+            l = torch.zeros_like(l).scatter_(-1, si, sl)
+        return F.softmax(l, -1)
+
+    g = torch.Generator().manual_seed(1)
+    counts = torch.zeros(4, 50)
+    n = 3000
+    for _ in range(n):
+        for r, t in enumerate(Sampler().sample_rows(logits, params, g)):
+            counts[r, t] += 1
+    for r in range(3):
+        ref = reference_probs(logits[r], params[r])
+        emp = counts[r] / n
+        assert torch.equal(emp > 0, ref > 0), r
+        assert (emp - ref).abs().max() < 0.03, r
+    assert counts[3, int(torch.argmax(logits[3]))] == n
+
+
 def test_model_config_from_hf_config():
     from transformers import LlamaConfig
 
