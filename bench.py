@@ -789,6 +789,7 @@ def run_engine(args, rank, world, local_rank):
     eng = LLMEngine.from_model(model, num_gpu_blocks=blocks, num_cpu_blocks=16, max_batch_size=B,
                                max_tokens_per_step=10 ** 9, mode="physical", dtype=dt, device=dev,
                                max_prefill_rows=16384)
+    eng.capture_decode_graphs()  # startup work, outside the timed region
     for p in prompts:
         eng.add_request(p, SamplingParams(temperature=0.0, max_tokens=steps + 1))
     torch.cuda.synchronize(dev)
@@ -861,13 +862,115 @@ def run_engine(args, rank, world, local_rank):
     return 0
 
 
+# ── config 4: mixed prefill + decode, sequence-sharded ───────────────────────
+
+C4 = ("Config 4: TinyLlama shape (config 0 model), 1024 requests, prompts "
+      "clip(round(lognormal(6,1)),16,4096), outputs U[16,512], FCFS, preemption when the pool "
+      "is 90% full, sequence-sharded (one engine per GPU, NCCL token gather)")
+
+
+def run_c4(args, rank, world, local_rank):
+    """All 1024 requests to completion; generated tokens per second over the whole run."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from vllm_mps_b200.core.sequence import SamplingParams
+    from vllm_mps_b200.engine.distributed import ShardedEngine
+    from vllm_mps_b200.engine.llm_engine import LLMEngine
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    nl, hid, nh, nkv, mlp, vocab, theta, dtn = ENGINE["c0"][:8]
+    cfg = LlamaConfig(hidden_size=hid, intermediate_size=mlp, num_hidden_layers=nl,
+                      num_attention_heads=nh, num_key_value_heads=nkv, vocab_size=vocab,
+                      rms_norm_eps=1e-5, rope_theta=theta, max_position_embeddings=8192,
+                      tie_word_embeddings=False)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg).to(torch.float16).eval()
+    rng = np.random.default_rng(4)
+    n_req = 1024
+    p_lens = np.clip(np.round(rng.lognormal(6, 1, n_req)), 16, 4096).astype(int)
+    o_lens = rng.integers(16, 513, n_req)
+    prompts = [rng.integers(0, vocab, size=int(n)).tolist() for n in p_lens]
+    params = [SamplingParams(temperature=0.0, max_tokens=int(m)) for m in o_lens]
+    eng = LLMEngine.from_model(model, num_gpu_blocks=16384, num_cpu_blocks=4096,
+                               max_batch_size=256, max_tokens_per_step=10 ** 9, mode="physical",
+                               preempt_watermark=0.9, dtype=torch.float16, device=dev,
+                               max_prefill_rows=16384)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    eng.capture_decode_graphs()  # startup work: every batch bucket up to 256
+    # Warm-up: a few requests through this rank's engine (workspaces, prefill path).
+    for p in prompts[:4]:
+        eng.add_request(p[:64], SamplingParams(temperature=0.0, max_tokens=8))
+    while not eng.is_finished():
+        eng.step()
+    torch.cuda.synchronize(dev)
+    start_tokens = eng.total_tokens_generated
+    if dist is not None:
+        dist.barrier(device_ids=[local_rank])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall = time.perf_counter()
+    with ClockSampler(dev.index or 0) as clocks:
+        e0.record()
+        if dist is not None:
+            sharded = ShardedEngine(eng)
+            sharded.add_requests(prompts, params)
+            outs = sharded.run()
+            done = sum(len(o.token_ids) for o in outs.values())
+            steps = sharded.steps
+        else:
+            for p, sp in zip(prompts, params):
+                eng.add_request(p, sp)
+            steps = 0
+            while not eng.is_finished():
+                eng.step()
+                steps += 1
+            done = eng.total_tokens_generated - start_tokens
+        e1.record()
+        torch.cuda.synchronize(dev)
+    t = e0.elapsed_time(e1) * 1e-3
+    if dist is not None:
+        tt = torch.tensor([t], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt[0])
+    from vllm_mps_b200 import kernels as K
+
+    if K.error_word(dev):
+        raise RuntimeError("device error word set during the config-4 run")
+    if done != int(o_lens.sum()):
+        raise RuntimeError(f"generated {done} tokens, expected {int(o_lens.sum())}")
+    if rank == 0:
+        line = {
+            "metric": "generated tokens/s (mixed prefill + decode)", "value": done / t,
+            "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": 1,
+            "ms_per_step": t / max(steps, 1) * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (random-init weights, seeded lognormal prompts)",
+            "config": {"workload": C4, "global_batch": n_req, "parallelism":
+                       f"sequence-sharded x{world}", "prompt_tokens": int(p_lens.sum()),
+                       "generated_tokens": int(o_lens.sum()), "wall_s": time.perf_counter() - t_wall,
+                       "preempted_final": eng.scheduler.get_num_preempted(),
+                       "timing": "CUDA events around the whole run, max over ranks"},
+            "e2e": {"value": done / t, "unit": "tokens/s", "h2d_bytes_per_step": None,
+                    "d2h_bytes_per_step": None,
+                    "api": "LLMEngine / ShardedEngine: host token ids in and out"},
+            "roofline": None, "clocks": clocks.summary(), "gpu_launches": None,
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PREFILL) + sorted(ENGINE),
+    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PREFILL) + sorted(ENGINE) + ["c4"],
                     default="c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -879,7 +982,7 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference" and cfg is not None:
         return run_reference(args, cfg, rank, world)
-    if args.impl == "reference" and args.config in ENGINE:
+    if args.impl == "reference" and (args.config in ENGINE or args.config == "c4"):
         if rank == 0:
             print(json.dumps({"impl": "reference", "unavailable":
                               "the reference engine is Python on its CPU path and does not travel "
@@ -895,6 +998,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.config == "c4":
+            return run_c4(args, rank, world, local_rank)
         if args.config in ENGINE:
             return run_engine(args, rank, world, local_rank)
         if cfg is None:

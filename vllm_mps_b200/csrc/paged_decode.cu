@@ -349,15 +349,20 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
   // q/k/v and the pool may still be being written by the previous kernel.
   if (p.early_prologue) pdl_wait();
   pdl_trigger();
-  if (blockIdx.x == 0) {
-    // Zero rows for empty sequences (they own no work unit, so in fused mode
-    // their new K/V is not written either: flagged).  One thread per sequence.
-    for (int s = tid; s < num_seqs; s += blockDim.x) {
-      if (pref[s + 1] == pref[s]) {
-        if (p.fused && p.slot_mapping[s] >= 0) set_error(p.err, kDevErrSlotNotLast);
-        T* o = static_cast<T*>(p.out) + static_cast<size_t>(s) * p.n_q * D;
-        for (int e = 0; e < p.n_q * D; ++e) o[e] = Elt<T>::from_f(0.f);
-      }
+  // Zero rows for empty sequences (they own no work unit, so in fused mode
+  // their new K/V is not written either: flagged).  The rows are spread over
+  // all CTAs, each written by the whole CTA with coalesced stores -- a
+  // padded batch can hold hundreds of them.
+  for (int s = blockIdx.x; s < num_seqs; s += gridDim.x) {
+    if (pref[s + 1] != pref[s]) continue;
+    if (tid == 0 && p.fused && p.slot_mapping[s] >= 0) set_error(p.err, kDevErrSlotNotLast);
+    T* o = static_cast<T*>(p.out) + static_cast<size_t>(s) * p.n_q * D;
+    if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+      uint4* o4 = reinterpret_cast<uint4*>(o);
+      const int n16 = p.n_q * D * static_cast<int>(sizeof(T)) / 16;
+      for (int e = tid; e < n16; e += blockDim.x) o4[e] = make_uint4(0u, 0u, 0u, 0u);
+    } else {
+      for (int e = tid; e < p.n_q * D; e += blockDim.x) o[e] = Elt<T>::from_f(0.f);
     }
   }
   if (u_begin >= u_end) return;

@@ -147,5 +147,18 @@ class DecodeGraphRunner:
         g.replay()
         return st.logits[:B]
 
+    def capture_all(self, max_batch: int) -> list[int]:
+        """Capture every bucket up to ``max_batch`` now (a serving engine's startup)."""
+        done = []
+        for b in BUCKETS:
+            if b > max(1, max_batch) and done:
+                break
+            if b not in self._graphs:
+                self._graphs[b] = self._capture(b)
+            done.append(b)
+            if b >= max_batch:
+                break
+        return done
+
     def release(self) -> None:
         self._graphs.clear()

@@ -128,6 +128,13 @@ class LLMEngine:
         eng.start_time = time.time()
         return eng
 
+    def capture_decode_graphs(self) -> list[int]:
+        """Capture the decode step's CUDA graph for every batch bucket up to
+        ``max_batch_size`` now instead of on first use; returns the buckets."""
+        if self._graphs is None:
+            return []
+        return self._graphs.capture_all(self.scheduler.max_batch_size)
+
     # ── requests ─────────────────────────────────────────────────────────────
 
     def add_request(self, prompt: str | list[int], sampling_params: SamplingParams | None = None) -> int:
@@ -253,7 +260,7 @@ class LLMEngine:
                 for pl in self.adapter.paged_layers:
                     pl.evict_sequence(seq_id)
             out = self._outputs[request_id]
-            out.token_ids = list(seq._output_token_ids)
+            out.token_ids.append(token_id)  # mirrors seq._output_token_ids
             if self.tokenizer is not None:
                 out.generated_text = self.tokenizer.decode(seq._output_token_ids,
                                                            skip_special_tokens=True)

@@ -118,7 +118,8 @@ class Scheduler:
             admitted.append(group)
 
         # 3. keep or preempt the groups that were already running (:163-187)
-        for group in [g for g in self._running if g not in scheduled]:
+        picked = {id(g) for g in scheduled}
+        for group in [g for g in self._running if id(g) not in picked]:
             seqs = group.get_seqs(SequenceStatus.RUNNING)
             if all(self._fits(s.seq_id, 1) for s in seqs):
                 scheduled.append(group)
@@ -133,8 +134,9 @@ class Scheduler:
                 preempted.append(group)
 
         # 4. one new slot per continuing sequence (:189-196)
+        fresh = {id(g) for g in admitted} | {id(g) for g in resumed}
         for group in scheduled:
-            if group in admitted or group in resumed:
+            if id(group) in fresh:
                 continue
             for s in group.get_seqs(SequenceStatus.RUNNING):
                 self.kv_cache_manager.append_slot(s.seq_id)
