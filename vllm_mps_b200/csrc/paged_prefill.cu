@@ -13,13 +13,14 @@
 // the G query heads that share the kv head, so every K/V tile loaded serves
 // all G heads (GQA is never materialised).  Key tiles are 64 keys (4 pages).
 //
-// Data movement.  Warp 4 (one lane) loads the Q tile with a 3-D TMA and the
-// K and V pages with 4-D TMAs (no multicast), all with the 128-byte swizzle,
-// into a K ring and a V ring of two tiles each, so K(j+2) loads as soon as
-// QK(j) is done and V(j+2) as soon as PV(j) is.  Pages past the sequence's
+// Data movement.  Warp 4 loads the Q tile with a 3-D TMA and the K pages,
+// warp 5 the V pages, with 4-D TMAs (no multicast), all with the 128-byte
+// swizzle, into a K ring and a V ring of two tiles each, so K(j+2) loads as
+// soon as QK(j) is done and V(j+2) as soon as PV(j) is, neither waiting on
+// the other.  Block ids are fetched 32 pages at a time, a batch ahead.  Pages past the sequence's
 // table are fetched at an out-of-range coordinate (the TMA fills zeros).
 //
-// Math.  Warp 5 (one lane) issues tcgen05.mma (kind::f16, M=128, fp32
+// Math.  Warp 6 (one lane) issues tcgen05.mma (kind::f16, M=128, fp32
 // accumulate).  S(j) = Q K(j)^T goes to one of two 64-column TMEM buffers,
 // so QK(j+1) runs while the softmax works on S(j).  The softmax warps write
 // P(j) as 16-bit pairs over the first 32 columns of S(j)'s own buffer and
@@ -48,7 +49,10 @@ constexpr int kPfRows = 128;       // MMA M: rows per tile
 constexpr int kPfKeys = 64;        // keys per key tile (4 pages)
 constexpr int kPfPages = kPfKeys / 16;
 constexpr int kPfStages = 2;       // K ring and V ring depth
-constexpr int kPfThreads = 192;    // warps 0-3 softmax, 4 loads, 5 MMA
+constexpr int kPfThreads = 224;    // warps 0-3 softmax, 4 K loads, 5 V loads, 6 MMA
+constexpr int kKWarp = 4;
+constexpr int kVWarp = 5;
+constexpr int kMmaWarp = 6;
 constexpr int kRegion = 128 * 128; // 128 rows x 64 16-bit columns (one swizzle span)
 constexpr int kKRegion = kPfKeys * 128;  // one 64-column chunk of a key tile
 
@@ -243,7 +247,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
                  "r"(Shape::kTmemCols)
@@ -255,86 +259,84 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 4) {
-    // ── loads: Q once, then K(j) and V(j) into their own rings ───────────────
-    if (lane == 0) {
+  if (warp == kKWarp || warp == kVWarp) {
+    // ── loads: one warp streams K tiles, another V tiles, so a K load never
+    // queues behind a V slot that PV has not released yet.  The block ids
+    // come 32 pages at a time (one coalesced load by the warp, the next batch
+    // fetched one batch ahead), handed to lane 0 with shuffles.
+    const bool is_v = warp == kVWarp;
+    if (!is_v && lane == 0) {
       prefetch_tmap(&q_map);
-      prefetch_tmap(&kv_map);
       mbar_arrive_expect_tx(q_full, Shape::kQBytes);
 #pragma unroll
       for (int c = 0; c < Shape::kChunks; ++c) {
         tma_load_3d(sQ + c * kRegion, &q_map, q_full, c * 64, kvh * p.G, row0 + tok0);
       }
-      const int32_t* table = p.block_tables + static_cast<size_t>(seq) * p.max_blocks;
-      const int n_pages = (n_keys + 15) >> 4;
-      const int oob = 2 * p.num_blocks;  // past the pool: the TMA fills zeros
-      int k_issued = 0, v_issued = 0;
-      for (int j = 0; j < n_key_tiles; ++j) {
-        const int st = j % kPfStages;
-        const uint32_t ph = ((j / kPfStages) - 1) & 1;
-        int blk[kPfPages];
+    }
+    if (lane == 0) prefetch_tmap(&kv_map);
+    const int32_t* table = p.block_tables + static_cast<size_t>(seq) * p.max_blocks;
+    const int n_pages = (n_keys + 15) >> 4;
+    const int oob = 2 * p.num_blocks;  // past the pool: the TMA fills zeros
+    auto fetch = [&](int page) -> int {  // block id of `page`, or -1
+      if (page >= n_pages) return -1;
+      if (page >= p.max_blocks) {
+        set_error(p.err, kDevErrSeqLen);
+        return -1;
+      }
+      const int b = table[page];
+      if (b < 0 || b >= p.num_blocks) {
+        set_error(p.err, kDevErrBlockRange);
+        return -1;
+      }
+      return b;
+    };
+    int ids = fetch(lane), nxt = fetch(32 + lane), batch = 0;
+    uint64_t* full = is_v ? v_full : k_full;
+    uint64_t* empty = is_v ? v_empty : k_empty;
+    uint8_t* ring = is_v ? sV : sK;
+    int issued = 0;
+    for (int j = 0; j < n_key_tiles; ++j) {
+      const int page0 = j * kPfPages;
+      if ((page0 >> 5) != batch) {
+        batch = page0 >> 5;
+        ids = nxt;
+        nxt = fetch((batch + 1) * 32 + lane);
+      }
+      int blk[kPfPages];
 #pragma unroll
-        for (int pg = 0; pg < kPfPages; ++pg) {
-          const int page = j * kPfPages + pg;
-          int b = -1;
-          if (page < n_pages) {
-            if (page < p.max_blocks) {
-              b = table[page];
-              if (b < 0 || b >= p.num_blocks) {
-                set_error(p.err, kDevErrBlockRange);
-                b = -1;
-              }
-            } else {
-              set_error(p.err, kDevErrSeqLen);
+      for (int pg = 0; pg < kPfPages; ++pg) blk[pg] = __shfl_sync(0xffffffffu, ids, (page0 + pg) & 31);
+      bool go = true;
+      if (lane == 0) {
+        const int st = j % kPfStages;
+        // Slot free once QK (K) or PV (V) of tile j - stages is done with it.
+        if (j >= kPfStages &&
+            (!mbar_wait(empty + st, ((j / kPfStages) - 1) & 1, p.err) || aborted(abort_flag))) {
+          *abort_flag = 1;
+          go = false;
+        } else {
+          mbar_arrive_expect_tx(full + st, Shape::kTileBytes);
+#pragma unroll
+          for (int pg = 0; pg < kPfPages; ++pg) {
+            const int coord = blk[pg] < 0 ? oob : 2 * blk[pg] + (is_v ? 1 : 0);
+#pragma unroll
+            for (int c = 0; c < Shape::kChunks; ++c) {
+              tma_load_4d(ring + st * Shape::kTileBytes + c * kKRegion + pg * 2048, &kv_map,
+                          full + st, c * 64, 0, kvh, coord);
             }
           }
-          blk[pg] = b;
+          issued = j + 1;
         }
-        // K(j) once QK(j - stages) is done with the slot.
-        if (j >= kPfStages && (!mbar_wait(k_empty + st, ph, p.err) || aborted(abort_flag))) {
-          *abort_flag = 1;
-          break;
-        }
-        mbar_arrive_expect_tx(k_full + st, Shape::kTileBytes);
-#pragma unroll
-        for (int pg = 0; pg < kPfPages; ++pg) {
-          const int ck = blk[pg] < 0 ? oob : 2 * blk[pg];
-#pragma unroll
-          for (int c = 0; c < Shape::kChunks; ++c) {
-            tma_load_4d(sK + st * Shape::kTileBytes + c * kKRegion + pg * 2048, &kv_map,
-                        k_full + st, c * 64, 0, kvh, ck);
-          }
-        }
-        k_issued = j + 1;
-        // V(j) once PV(j - stages) is done with the slot.
-        if (j >= kPfStages && (!mbar_wait(v_empty + st, ph, p.err) || aborted(abort_flag))) {
-          *abort_flag = 1;
-          break;
-        }
-        mbar_arrive_expect_tx(v_full + st, Shape::kTileBytes);
-#pragma unroll
-        for (int pg = 0; pg < kPfPages; ++pg) {
-          const int cv = blk[pg] < 0 ? oob : 2 * blk[pg] + 1;
-#pragma unroll
-          for (int c = 0; c < Shape::kChunks; ++c) {
-            tma_load_4d(sV + st * Shape::kTileBytes + c * kKRegion + pg * 2048, &kv_map,
-                        v_full + st, c * 64, 0, kvh, cv);
-          }
-        }
-        v_issued = j + 1;
       }
-      if (aborted(abort_flag)) {
-        // Let this CTA's own loads land before its shared memory is released.
-        mbar_wait(q_full, 0, p.err);
-        for (int j = max(0, k_issued - kPfStages); j < k_issued; ++j) {
-          mbar_wait(k_full + (j % kPfStages), (j / kPfStages) & 1, p.err);
-        }
-        for (int j = max(0, v_issued - kPfStages); j < v_issued; ++j) {
-          mbar_wait(v_full + (j % kPfStages), (j / kPfStages) & 1, p.err);
-        }
+      if (!__shfl_sync(0xffffffffu, go ? 1 : 0, 0)) break;
+    }
+    if (lane == 0 && aborted(abort_flag)) {
+      // Let this warp's own loads land before the shared memory is released.
+      if (!is_v) mbar_wait(q_full, 0, p.err);
+      for (int j = max(0, issued - kPfStages); j < issued; ++j) {
+        mbar_wait(full + (j % kPfStages), (j / kPfStages) & 1, p.err);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ── MMA issue ─────────────────────────────────────────────────────────────
     // Order: QK(0), QK(1), then per tile j: PV(j) [after the softmax of j],
     // QK(j + 2) into the S buffer PV(j) just read P from (MMAs of one thread
@@ -524,7 +526,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(Shape::kTmemCols)
