@@ -62,6 +62,19 @@ namespace vmps {
 constexpr int kStages = VMPS_DECODE_STAGES;
 constexpr int kCtasPerSm = VMPS_DECODE_CTAS_PER_SM;
 constexpr int kMinPagesPerCta = 4;
+// Work is split in a weighted page space: a page weighs kPageWeight and every
+// non-empty sequence adds kSegmentWeight before its first page: the extra
+// cost a CTA pays to start a sequence (query rows, RoPE tables, its own
+// accumulators, the partial store of a split piece; ~2 us per extra sequence
+// measured in a CTA; a sweep of the weight on C1 was best at 9 pages).
+// CTA b owns the pages whose weighted position lies in
+// [b*wchunk, (b+1)*wchunk), so CTAs whose chunk spans several sequences get
+// fewer pages and all CTAs finish together.
+#ifndef VMPS_DECODE_SEG_WEIGHT
+#define VMPS_DECODE_SEG_WEIGHT 36
+#endif
+constexpr int kPageWeight = 4;
+constexpr int kSegmentWeight = VMPS_DECODE_SEG_WEIGHT;
 constexpr int kMaxSeqs = 4096;
 constexpr int kMaxKvHeads = 64;
 #ifndef VMPS_DECODE_SEG_TABLES
@@ -253,6 +266,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
   const uint32_t ring_off = ((dyn_base + 1023u) & ~1023u) - dyn_base;
   uint8_t* ring = dyn_smem + ring_off;
   int* pref = reinterpret_cast<int*>(ring + kStages * Shape::kStageBytes);
+  int* wpref = pref + (num_seqs + 1);  // weighted prefix sums
 
   if (tid == 0) {
     s_abort = 0;
@@ -277,31 +291,64 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
       pages = p.max_blocks;
     }
     pref[s + 1] = pages;
+    wpref[s + 1] = pages > 0 ? pages * kPageWeight + kSegmentWeight : 0;
   }
-  if (tid == 0) pref[0] = 0;
+  if (tid == 0) {
+    pref[0] = 0;
+    wpref[0] = 0;
+  }
   __syncthreads();
   if (warp == 0) {
-    int carry = 0;
+    int carry = 0, wcarry = 0;
     for (int base = 0; base < num_seqs; base += 32) {
       const int s = base + lane;
       int v = s < num_seqs ? pref[s + 1] : 0;
+      int w = s < num_seqs ? wpref[s + 1] : 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int y = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += y;
+        const int z = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) {
+          v += y;
+          w += z;
+        }
       }
-      if (s < num_seqs) pref[s + 1] = v + carry;
+      if (s < num_seqs) {
+        pref[s + 1] = v + carry;
+        wpref[s + 1] = w + wcarry;
+      }
       carry += __shfl_sync(0xffffffffu, v, 31);
+      wcarry += __shfl_sync(0xffffffffu, w, 31);
     }
   }
   __syncthreads();
 
   const int TP = pref[num_seqs];
+  const int WTP = wpref[num_seqs];
   const long long U = static_cast<long long>(p.num_hg) * TP;
-  long long chunk = (U + p.n_cta - 1) / p.n_cta;
-  if (chunk < kMinPagesPerCta) chunk = kMinPagesPerCta;
-  const long long u_begin = static_cast<long long>(blockIdx.x) * chunk;
-  const long long u_end = u_begin + chunk < U ? u_begin + chunk : U;
+  const long long WU = static_cast<long long>(p.num_hg) * WTP;
+  long long wchunk = (WU + p.n_cta - 1) / p.n_cta;
+  if (wchunk < kMinPagesPerCta * kPageWeight) wchunk = kMinPagesPerCta * kPageWeight;
+  // First page unit whose weighted position is >= w.
+  auto unit_at = [&](long long w) -> long long {
+    if (w >= WU) return U;
+    const int hg = static_cast<int>(w / WTP);
+    const int wf = static_cast<int>(w - static_cast<long long>(hg) * WTP);
+    const int s = upper_bound_pref(wpref, num_seqs, wf);
+    const int pages = pref[s + 1] - pref[s];
+    int pg = (wf - wpref[s] - kSegmentWeight + kPageWeight - 1) / kPageWeight;
+    if (wf - wpref[s] <= kSegmentWeight) pg = 0;
+    if (pg > pages) pg = pages;
+    return static_cast<long long>(hg) * TP + pref[s] + pg;
+  };
+  // The CTA that owns page `pg` of sequence s in head group hg.
+  auto owner_cta = [&](int hg, int s, int pg) -> int {
+    const long long w = static_cast<long long>(hg) * WTP + wpref[s] + kSegmentWeight +
+                        static_cast<long long>(pg) * kPageWeight;
+    return static_cast<int>(w / wchunk);
+  };
+  const long long u_begin = unit_at(static_cast<long long>(blockIdx.x) * wchunk);
+  const long long u_end = unit_at(static_cast<long long>(blockIdx.x + 1) * wchunk);
 
   // Work decode for a unit: its head group and physical block (producer) or
   // its sequence (consumers).
@@ -718,9 +765,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
       // Split sequence: publish this piece now; the arrival (and the merge,
       // for the last piece) waits until this CTA's pages are all streamed,
       // so a round trip to the counter never stalls the page pipeline.
-      const long long seg_first = static_cast<long long>(hg) * TP + pref[s];
-      const int c0 = static_cast<int>(seg_first / chunk);
-      const int c1 = static_cast<int>((seg_first + seg_pages - 1) / chunk);
+      const int c0 = owner_cta(hg, s, 0);
+      const int c1 = owner_cta(hg, s, seg_pages - 1);
       const int slot = (static_cast<int>(blockIdx.x) == c0) ? 1 : 0;
       const size_t rec = (static_cast<size_t>(blockIdx.x) * 2 + slot) * HPC + h;
       float4* po = reinterpret_cast<float4*>(p.part_o) + rec * NT * KS * 32;
@@ -905,7 +951,7 @@ static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 template <typename T, int D, int HPC, int NT>
 static int launch_decode(const CUtensorMap& tmap, const DecodeParams& p, cudaStream_t s) {
   using Shape = DecodeShape<D, HPC>;
-  const size_t smem = 1024 + kStages * Shape::kStageBytes + (p.num_seqs + 1) * sizeof(int);
+  const size_t smem = 1024 + kStages * Shape::kStageBytes + 2 * (p.num_seqs + 1) * sizeof(int);
   static std::once_flag flags[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -913,7 +959,7 @@ static int launch_decode(const CUtensorMap& tmap, const DecodeParams& p, cudaStr
   std::call_once(flags[dev], [] {
     cudaFuncSetAttribute(paged_decode_kernel<T, D, HPC, NT>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         1024 + kStages * Shape::kStageBytes + (kMaxSeqs + 1) * sizeof(int));
+                         1024 + kStages * Shape::kStageBytes + 2 * (kMaxSeqs + 1) * sizeof(int));
   });
   const cudaError_t e = launch_pdl(paged_decode_kernel<T, D, HPC, NT>, dim3(p.n_cta),
                                    dim3(Shape::kThreads), smem, s, tmap, p);
