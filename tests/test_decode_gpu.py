@@ -340,3 +340,36 @@ def test_fused_attention_reference_api(cuda_device):
     torch.cuda.synchronize()
     np.testing.assert_allclose(O.bits_to_f32(_bits(out), dt), O.bits_to_f32(d["attn_out"], dt),
                                atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("shape", [
+    # name, n_q, n_kv, D, dtype, context lengths
+    ("one long among many one-page", 32, 4, 64, "float16", [4000] + [5] * 200),
+    ("mostly empty (a padded graph bucket)", 32, 4, 64, "float16",
+     [0] * 150 + [700, 1, 1300] + [0] * 100 + [64]),
+    ("4096 tiny sequences", 32, 4, 64, "float16", [1 + (i * 7) % 16 for i in range(4096)]),
+    ("G=16, head_dim 128, ragged", 64, 4, 128, "bfloat16", [(i * 977) % 3000 + 1 for i in range(40)]),
+])
+def test_work_split_extremes(cuda_device, shape):
+    """The cost-weighted split over pages and sequence starts at its extremes:
+    outputs against fp32 attention, merge counters left at zero (a second
+    call on the same workspace gives identical bits), no error bits."""
+    from vllm_mps_b200 import kernels as K
+
+    name, n_q, n_kv, D, dt, ctx = shape
+    pages = sum((c + 15) // 16 for c in ctx)
+    c = _seeded_case(77, len(ctx), n_q, n_kv, D, dt, 0, 0, pages + 64, cuda_device, ctx=ctx,
+                     pool_on_device=True)
+    ws = K.DecodeWorkspace()
+    out = K.paged_decode_attention(c["q"], c["pool"], c["bt"], c["sl"], workspace=ws)
+    out2 = K.paged_decode_attention(c["q"], c["pool"], c["bt"], c["sl"], workspace=ws)
+    torch.cuda.synchronize()
+    assert K.error_word(cuda_device) == 0, name
+    assert torch.equal(out.view(torch.int16), out2.view(torch.int16)), name
+    nz = [i for i, L in enumerate(ctx) if L > 0]
+    z = [i for i, L in enumerate(ctx) if L == 0]
+    if z:
+        assert torch.count_nonzero(out[z]) == 0
+    ref = _torch_fp32_attention(c["q"][nz], c["pool"], c["bt_np"][nz], np.array(ctx)[nz])
+    atol, rtol = _tol(dt)
+    torch.testing.assert_close(out[nz].float(), ref, atol=atol, rtol=rtol)
