@@ -549,6 +549,10 @@ PREFILL = {
     "prefill": (16, 2048, 32, 8, 128, "bfloat16", 500000.0,
                 "Causal paged prefill, Llama-3-8B attention shape: 16 prompts x 2048 tokens, "
                 "32 q / 8 kv heads, head_dim 128, bf16, block_size 16, permuted pool"),
+    # TinyLlama attention shape (configs 0 and 4), fp16.
+    "prefill_tinyllama": (16, 2048, 32, 4, 64, "float16", 10000.0,
+                          "Causal paged prefill, TinyLlama attention shape: 16 prompts x 2048 "
+                          "tokens, 32 q / 4 kv heads, head_dim 64, fp16, block_size 16, permuted pool"),
 }
 
 
@@ -716,11 +720,12 @@ def run_prefill(args, rank, world, local_rank):
             "metric": "prefill tokens/s", "value": world * rows * args.steps / t,
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16",
+            "vs_baseline": None, "dtype": "bf16" if dt == torch.bfloat16 else "f16",
             "data": "synthetic (seeded N(0,1) q/k/v/pool)",
             "config": {"workload": desc, "global_batch": B * world, "seq_len": L,
                        "parallelism": f"sequence-sharded x{world}",
-                       "l2": "inputs larger than L2 (q 268 MB, out 268 MB, K/V 134 MB per rank)",
+                       "l2": f"inputs larger than L2 (q {rows * n_q * D * 2 / 1e6:.0f} MB, out the "
+                             f"same, K/V {B * L * n_kv * D * 4 / 1e6:.0f} MB per rank)",
                        "timing": "back-to-back launches, CUDA events, max over ranks"},
             "e2e": {"value": world * rows * e2e_steps / t_e2e, "unit": "tokens/s",
                     "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in (hq, hk, hv)),
