@@ -54,6 +54,10 @@ CONFIGS = {
     "c1": (64, 32, 4, 64, "float16", 1, 2048, 16384, 8,
            "C1 single-layer paged decode step: batch 64, 32 q / 4 kv heads, head_dim 64, "
            "fp16, ctx U[1,2048], block_size 16, permuted 16384-block pool"),
+    "c2layer": (256, 32, 8, 128, "bfloat16", 128, 4224, 36000, 2,
+                "C2 single layer: Llama-3-8B attention (32 q / 8 kv heads, head_dim 128), bf16, "
+                "batch 256, ctx U[128,4224] (prompts U[128,4096] + 128 steps), block_size 16, "
+                "permuted 36000-block pool"),
     "c3": (4, 64, 8, 128, "float16", 131072, 131072, 32768 + 64, 2,
            "C3 long-context split-K decode: batch 4 x 131072, 64 q / 8 kv heads, "
            "head_dim 128, fp16, permuted 32832-block pool"),
@@ -262,7 +266,8 @@ def run_reference(args, cfg, rank, world):
     line = {
         "metric": "decode tokens/s", "value": val, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if dt == "bfloat16" else "f16",
         "data": "synthetic (seeded)", "impl": "reference",
         "config": {"workload": desc, "global_batch": B, "parallelism": "host cores"},
         "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": c_oracle.max_threads(),
@@ -509,7 +514,7 @@ def run_ours(args, cfg, rank, world, local_rank):
             "metric": "decode tokens/s", "value": world * B * args.steps / t_step,
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": t_step / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if dt == "bfloat16" else "f16",
             "data": "synthetic (seeded N(0,1) q/k/v/pool; seeded ragged contexts)",
             "config": {
                 "workload": desc, "global_batch": B * world, "seq_len": "U[%d,%d]" % (lo, hi),

@@ -349,6 +349,8 @@ def test_fused_attention_reference_api(cuda_device):
      [0] * 150 + [700, 1, 1300] + [0] * 100 + [64]),
     ("4096 tiny sequences", 32, 4, 64, "float16", [1 + (i * 7) % 16 for i in range(4096)]),
     ("G=16, head_dim 128, ragged", 64, 4, 128, "bfloat16", [(i * 977) % 3000 + 1 for i in range(40)]),
+    ("64 kv heads (the supported maximum), MHA", 64, 64, 64, "float16",
+     [(i * 311) % 900 + 1 for i in range(24)]),
 ])
 def test_work_split_extremes(cuda_device, shape):
     """The cost-weighted split over pages and sequence starts at its extremes:
