@@ -229,3 +229,13 @@ def test_model_config_from_hf_config():
     cfg = ModelConfig.from_hf_config(hf, "llama3-shape", device="cpu")
     assert (cfg.n_heads, cfg.n_kv_heads, cfg.d_k, cfg.architecture) == (32, 8, 128, "llama")
     assert cfg.rope_theta == 500000.0 and cfg.get_kv_cache_config()["n_heads"] == 8
+
+
+def test_decode_graph_buckets():
+    """Batch sizes map to the smallest bucket that holds them; larger batches run eagerly."""
+    from vllm_mps_b200.engine.decode_graph import BUCKETS, DecodeGraphRunner
+
+    assert [DecodeGraphRunner.bucket(b) for b in (1, 2, 3, 8, 9, 256, 257, 512)] == \
+        [1, 2, 4, 8, 16, 256, 512, 512]
+    assert DecodeGraphRunner.bucket(BUCKETS[-1] + 1) is None
+    assert list(BUCKETS) == sorted(BUCKETS)
