@@ -239,3 +239,18 @@ def test_decode_graph_buckets():
         [1, 2, 4, 8, 16, 256, 512, 512]
     assert DecodeGraphRunner.bucket(BUCKETS[-1] + 1) is None
     assert list(BUCKETS) == sorted(BUCKETS)
+
+
+def test_model_config_from_a_local_checkpoint_directory(tmp_path):
+    """from_pretrained reads a saved config (no network): the way a user points the
+    engine at a local model (core/model_config.py:50-96 of the reference)."""
+    from transformers import LlamaConfig
+
+    from vllm_mps_b200.core.model_config import ModelConfig
+
+    LlamaConfig(hidden_size=256, num_attention_heads=8, num_key_value_heads=2,
+                num_hidden_layers=3, vocab_size=1000, rope_theta=250000.0,
+                max_position_embeddings=4096, architectures=["LlamaForCausalLM"]).save_pretrained(tmp_path)
+    cfg = ModelConfig.from_pretrained(str(tmp_path))
+    assert (cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.d_k, cfg.n_layers) == (256, 8, 2, 32, 3)
+    assert cfg.architecture == "llama" and cfg.rope_theta == 250000.0 and cfg.max_seq_len == 4096
