@@ -770,9 +770,10 @@ def run_engine(args, rank, world, local_rank):
     Every rank runs its own engine on its own requests (sequence sharding,
     weak scaling).  The timed region is the decode steps after the first
     step (which also prefills every prompt), each one the engine's public
-    ``step()``: host token ids in, metadata built and copied, 22/32 layers
-    each with one fused decode-step kernel, greedy sampling, host token ids
-    out.
+    ``step()``: host token ids in, metadata built and copied, one CUDA-graph
+    replay (22/32 layers, each with the fused decode-step kernel and the fused
+    residual/RMSNorm/SiLU kernels between cuBLAS GEMMs), greedy sampling,
+    host token ids out.
     """
     import torch
     from transformers import LlamaConfig, LlamaForCausalLM
@@ -800,6 +801,7 @@ def run_engine(args, rank, world, local_rank):
                                max_tokens_per_step=10 ** 9, mode="physical", dtype=dt, device=dev,
                                max_prefill_rows=16384)
     eng.capture_decode_graphs()  # startup work, outside the timed region
+    fused = eng._graphs is not None and eng._graphs.fused
     for p in prompts:
         eng.add_request(p, SamplingParams(temperature=0.0, max_tokens=steps + 1))
     torch.cuda.synchronize(dev)
@@ -861,7 +863,10 @@ def run_engine(args, rank, world, local_rank):
                          "kernel": "whole decode step (weights + every layer's K/V history)",
                          "alg_bytes_per_step": step_bytes},
             "clocks": clocks.summary(),
-            "gpu_launches": n_timed * nl,
+            # Per step: the fused decode-step kernel per layer, plus (fused
+            # Llama layers) two add_rmsnorm + one silu_mul per layer and the
+            # first layer's input norm; the GEMMs are cuBLAS.
+            "gpu_launches": n_timed * (4 * nl + 1 if fused else nl),
             "cpu_baseline": None,
             "cpu_baseline_note": "the reference's engine is Python on its CPU path; config 0 "
                                  "took 33 tokens/s on 8 host cores in the survey (config 2 is "

@@ -209,6 +209,24 @@ int vmps_paged_prefill_attention(void* out, const void* q, int64_t q_row_stride,
                                  void* stream);
 
 /*
+ * Element-wise work between the GEMMs of a Llama decoder layer, fused for
+ * the CUDA-graph decode step.  No kernel counterpart in the reference, which
+ * runs these as HuggingFace modules (LlamaRMSNorm, the residual additions of
+ * LlamaDecoderLayer, SiLU(gate) * up of LlamaMLP); the rounding points of
+ * those modules are kept.
+ *
+ * vmps_add_rmsnorm: residual <- residual + delta (delta may be NULL), then
+ *   out <- weight * (residual * rsqrt(mean(residual^2) + eps)) for `rows`
+ *   rows of `hidden` elements (hidden % 8 == 0; rows 16-byte aligned).
+ * vmps_silu_mul: out[:, :inter] <- silu(gate_up[:, :inter]) * gate_up[:, inter:2*inter].
+ */
+int vmps_add_rmsnorm(void* out, int64_t out_row_stride, void* residual, int64_t res_row_stride,
+                     const void* delta, int64_t delta_row_stride, const void* weight, int rows,
+                     int hidden, float eps, int dtype, void* stream);
+int vmps_silu_mul(void* out, int64_t out_row_stride, const void* gate_up,
+                  int64_t in_row_stride, int rows, int inter, int dtype, void* stream);
+
+/*
  * Reads and clears the device error word of the current device (a bitwise OR
  * of index violations the kernels skipped since the last call).  Synchronises
  * `stream`.  Bits: 1 slot out of range, 2 block id out of range, 4 seq_len

@@ -241,6 +241,31 @@ def test_decode_graph_buckets():
     assert list(BUCKETS) == sorted(BUCKETS)
 
 
+def test_decode_graph_fused_layer_eligibility():
+    """A stock HF Llama takes the fused element-wise path (its SiLU is transformers'
+    own activation class); a model whose MLP is not SiLU-gated replays HF modules."""
+    from types import SimpleNamespace
+
+    import torch.nn as nn
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from vllm_mps_b200.engine.decode_graph import DecodeGraphRunner
+
+    cfg = LlamaConfig(hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, vocab_size=100)
+    model = LlamaForCausalLM(cfg).eval()
+    r = DecodeGraphRunner.__new__(DecodeGraphRunner)
+    r.adapter = SimpleNamespace(hf_model=model, model_config=SimpleNamespace(d_model=64))
+    assert r._llama_layers()
+    w_gate = model.model.layers[1].mlp.gate_proj.weight.detach().clone()
+    fused = r._fuse_gate_up()
+    assert fused[1].shape == (256, 64) and torch.equal(fused[1][:128], w_gate)
+    # The module weights are views of the fused buffer: one copy of the weights.
+    assert model.model.layers[1].mlp.up_proj.weight.data_ptr() == fused[1][128:].data_ptr()
+    model.model.layers[0].mlp.act_fn = nn.GELU()
+    assert not r._llama_layers()
+
+
 def test_model_config_from_a_local_checkpoint_directory(tmp_path):
     """from_pretrained reads a saved config (no network): the way a user points the
     engine at a local model (core/model_config.py:50-96 of the reference)."""

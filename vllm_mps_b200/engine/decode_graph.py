@@ -9,11 +9,15 @@ every decoder layer (RMSNorm, fused QKV GEMM, the fused decode-step kernel,
 O projection, RMSNorm, gated MLP, residuals), final norm and LM head -- is
 captured once per batch bucket as a CUDA graph and replayed.
 
-The forward replayed is the decoder layer's own sequence of HF submodules
-(``input_layernorm``, attention, residual, ``post_attention_layernorm``,
-``mlp``, residual; transformers' LlamaDecoderLayer.forward), minus the model
-level work a decode step does not use (masks and rotary tables: RoPE runs
-inside the decode kernel), so the logits are those of the eager path.
+For Llama-family layers (RMSNorm, bias-free SiLU-gated MLP) the replayed
+forward is 8 kernels per layer: the QKV GEMM, the fused decode-step kernel,
+the O GEMM, residual add + RMSNorm (``kernels.add_rmsnorm``), one [gate|up]
+GEMM (the two weights are re-pointed as views into one buffer), SiLU * up
+(``kernels.silu_mul``), the down GEMM, and residual add + the next RMSNorm --
+the ops of transformers' LlamaDecoderLayer / LlamaRMSNorm / LlamaMLP with
+their rounding points, minus the model-level work a decode step does not use
+(masks and rotary tables: RoPE runs inside the decode kernel).  Other models
+replay the HF submodules in the same order.
 
 Per step the host packs block tables, lengths, positions, slots and token ids
 of the batch, padded to the bucket (padding rows have length 0 and no slot:
@@ -51,6 +55,49 @@ class DecodeGraphRunner:
         self.device = adapter.model_config.device
         self._graphs: dict[int, tuple] = {}
         self._pool = None
+        self._gate_up = self._fuse_gate_up() if self._llama_layers() else None
+
+    def _llama_layers(self) -> bool:
+        """Whether every layer is RMSNorm + bias-free SiLU-gated MLP (the fused path)."""
+        import torch.nn as nn
+
+        m = self.adapter.hf_model.model
+        hid = self.adapter.model_config.d_model
+        for layer in m.layers:
+            mlp = getattr(layer, "mlp", None)
+            for name in ("input_layernorm", "post_attention_layernorm"):
+                if not hasattr(getattr(layer, name, None), "variance_epsilon"):
+                    return False
+            if mlp is None or not all(hasattr(mlp, a) for a in ("gate_proj", "up_proj", "down_proj")):
+                return False
+            act = getattr(mlp, "act_fn", None)
+            # transformers' SiLU is its own module class (SiLUActivation).
+            if not (isinstance(act, nn.SiLU) or type(act).__name__ == "SiLUActivation"):
+                return False
+            if any(getattr(mlp, a).bias is not None for a in ("gate_proj", "up_proj")):
+                return False
+            if mlp.gate_proj.out_features % 8 or hid % 8:
+                return False
+        return hasattr(m.norm, "variance_epsilon")
+
+    def _fuse_gate_up(self) -> list[torch.Tensor]:
+        """One [gate; up] weight per layer; the modules' weights become views of it."""
+        import torch.nn as nn
+
+        fused = []
+        for layer in self.adapter.hf_model.model.layers:
+            g, u = layer.mlp.gate_proj, layer.mlp.up_proj
+            w = torch.cat([g.weight.detach(), u.weight.detach()], 0).contiguous()
+            inter = g.out_features
+            g.weight = nn.Parameter(w[:inter], requires_grad=False)
+            u.weight = nn.Parameter(w[inter:], requires_grad=False)
+            fused.append(w)
+        return fused
+
+    @property
+    def fused(self) -> bool:
+        """Whether the replayed step uses the fused element-wise kernels."""
+        return self._gate_up is not None
 
     @staticmethod
     def bucket(batch: int) -> int | None:
@@ -62,6 +109,8 @@ class DecodeGraphRunner:
     # ── one step of the model on the static buffers ──────────────────────────
 
     def _forward(self, st) -> None:
+        if self._gate_up is not None:
+            return self._forward_fused(st)
         m = self.adapter.hf_model
         meta = st.meta
         x = m.model.embed_tokens(st.tokens).unsqueeze(1)
@@ -74,6 +123,28 @@ class DecodeGraphRunner:
             x = r + layer.mlp(h)
         x = m.model.norm(x)
         st.logits.copy_(m.lm_head(x[:, 0, :]))
+
+    def _forward_fused(self, st) -> None:
+        """Per layer: QKV GEMM, decode-step kernel, O GEMM, add+RMSNorm,
+        [gate|up] GEMM, SiLU*up, down GEMM, add+RMSNorm (the next layer's input
+        norm, or the final norm) -- 8 kernels."""
+        from vllm_mps_b200.kernels import add_rmsnorm, silu_mul
+
+        m = self.adapter.hf_model
+        layers = m.model.layers
+        res = m.model.embed_tokens(st.tokens)  # (Bb, d): the residual stream
+        h = torch.empty_like(res)
+        first = layers[0].input_layernorm
+        add_rmsnorm(res, first.weight, first.variance_epsilon, out=h)
+        for i, layer in enumerate(layers):
+            attn = layer.self_attn._attend(h.unsqueeze(1), st.meta)
+            post = layer.post_attention_layernorm
+            add_rmsnorm(res, post.weight, post.variance_epsilon, delta=attn.view_as(res), out=h)
+            act = silu_mul(torch.matmul(h, self._gate_up[i].t()))
+            mlp_out = layer.mlp.down_proj(act)
+            nxt = layers[i + 1].input_layernorm if i + 1 < len(layers) else m.model.norm
+            add_rmsnorm(res, nxt.weight, nxt.variance_epsilon, delta=mlp_out, out=h)
+        st.logits.copy_(m.lm_head(h))
 
     def _static(self, Bb: int):
         """Static buffers of a bucket: [tables Bb x W | lengths | positions | slots | tokens]."""

@@ -51,6 +51,8 @@ EXPORTED_SYMBOLS = (
     "vmps_paged_decode_attention",
     "vmps_paged_decode_step",
     "vmps_paged_prefill_attention",
+    "vmps_add_rmsnorm",
+    "vmps_silu_mul",
     "vmps_debug_error_word",
 )
 
@@ -95,6 +97,10 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.vmps_paged_prefill_attention.argtypes = [
             vp, vp, i64, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32,
             f32, i32, vp]
+        lib.vmps_add_rmsnorm.restype = i32
+        lib.vmps_add_rmsnorm.argtypes = [vp, i64, vp, i64, vp, i64, vp, i32, i32, f32, i32, vp]
+        lib.vmps_silu_mul.restype = i32
+        lib.vmps_silu_mul.argtypes = [vp, i64, vp, i64, i32, i32, i32, vp]
         lib.vmps_debug_error_word.restype = i32
         lib.vmps_debug_error_word.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
         if path is None:
@@ -400,6 +406,74 @@ def paged_prefill_attention(q: torch.Tensor, pool: torch.Tensor, block_tables: t
             int(max_q_len), n_q, n_kv, D, block_size, num_blocks, float(scale),
             dtype_code(pool.dtype), _stream(dev))
     _check(rc, "paged_prefill_attention")
+    return out
+
+
+# ── decoder-layer element-wise kernels (CUDA-graph decode step) ─────────────
+
+
+def _row_stride(t: torch.Tensor, cols: int, name: str) -> int:
+    if t.dim() != 2 or t.shape[1] < cols or t.stride(1) != 1:
+        raise ValueError(f"{name} must be 2-D (rows, >= {cols}) with unit inner stride")
+    return t.stride(0)
+
+
+def add_rmsnorm(residual: torch.Tensor, weight: torch.Tensor, eps: float,
+                delta: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """``residual += delta`` in place (when given), then ``out = RMSNorm(residual)``.
+
+    The residual addition and RMSNorm of transformers' LlamaDecoderLayer /
+    LlamaRMSNorm in one kernel (same rounding points: the sum rounded to the
+    dtype, the variance in fp32, the normalised value rounded before the
+    weight product).  ``residual``/``delta``/``out``: (rows, hidden), hidden a
+    multiple of 8; ``weight``: (hidden,).  Returns ``out``.
+    """
+    hidden = weight.numel()
+    rs = _row_stride(residual, hidden, "residual")
+    if residual.shape[1] != hidden:
+        raise ValueError(f"residual has {residual.shape[1]} columns, weight {hidden}")
+    for t, name in ((delta, "delta"), (out, "out")):
+        if t is not None and (t.shape != residual.shape or t.dtype != residual.dtype):
+            raise ValueError(f"{name} must match residual's shape and dtype")
+    if weight.dtype != residual.dtype or not weight.is_contiguous():
+        raise ValueError("weight must be contiguous with residual's dtype")
+    if out is None:
+        out = torch.empty_like(residual)
+    dev = _require_cuda(residual, weight, delta, out)
+    ds = _row_stride(delta, hidden, "delta") if delta is not None else 0
+    os_ = _row_stride(out, hidden, "out")
+    lib = load_library()
+    with torch.cuda.device(dev):
+        rc = lib.vmps_add_rmsnorm(_ptr(out), os_, _ptr(residual), rs, _ptr(delta), ds,
+                                  _ptr(weight), residual.shape[0], hidden, float(eps),
+                                  dtype_code(residual.dtype), _stream(dev))
+    _check(rc, "add_rmsnorm")
+    return out
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``silu(gate_up[:, :I]) * gate_up[:, I:]`` for a fused [gate | up] GEMM output.
+
+    LlamaMLP's ``act_fn(gate_proj(x)) * up_proj(x)`` after one GEMM of the
+    concatenated weights; silu rounded to the dtype before the product, as
+    the module does.  ``gate_up``: (rows, 2*I), I a multiple of 8.  Returns
+    ``out`` (rows, I).
+    """
+    if gate_up.dim() != 2 or gate_up.shape[1] % 2:
+        raise ValueError("gate_up must be (rows, 2 * inter)")
+    rows, inter = gate_up.shape[0], gate_up.shape[1] // 2
+    ins = _row_stride(gate_up, 2 * inter, "gate_up")
+    if out is None:
+        out = torch.empty((rows, inter), dtype=gate_up.dtype, device=gate_up.device)
+    elif out.shape != (rows, inter) or out.dtype != gate_up.dtype:
+        raise ValueError("out must be (rows, inter) of gate_up's dtype")
+    dev = _require_cuda(gate_up, out)
+    lib = load_library()
+    with torch.cuda.device(dev):
+        rc = lib.vmps_silu_mul(_ptr(out), _row_stride(out, inter, "out"), _ptr(gate_up), ins,
+                               rows, inter, dtype_code(gate_up.dtype), _stream(dev))
+    _check(rc, "silu_mul")
     return out
 
 
