@@ -32,8 +32,8 @@
 //    to kernel 1's.
 //  * A sequence cut between CTAs: every piece stores its fp32 state (running
 //    max, sum, unnormalised output in MMA-fragment order) and arrives on an
-//    atomic counter per kv head and sequence (release fence + relaxed add,
-//    issued a couple of pages later so it never stalls the page pipeline).
+//    atomic counter per kv head and sequence (one acq_rel add, issued a
+//    couple of pages later so it never stalls the page pipeline).
 //    The last piece to arrive stages all pieces into the freed shared-memory
 //    ring with cp.async (one round trip) and merges them.  Nobody waits on
 //    anybody.
@@ -42,8 +42,12 @@
 //    so a segment switch never waits on a global load queued behind the page
 //    stream.
 //  * Launched with programmatic dependent launch: in the fused step the
-//    prologue (page prefix sums, the first block-table entries, the first
-//    RoPE table) runs while the previous kernel in the stream finishes.
+//    prologue (page prefix sums, the first block-table entries, the loads of
+//    the first segments' lengths, slots and RoPE inputs) runs while the
+//    previous kernel in the stream finishes.  The producer's first page load
+//    waits for nothing but its block-table entries; the consumers' prologue
+//    overlaps it, with every global load issued before the first use, so a
+//    CTA placed just as the previous kernel ends starts streaming at once.
 #include <mutex>
 #include <utility>
 
@@ -116,16 +120,13 @@ struct DecodeParams {
   int* err;
 };
 
-__device__ __forceinline__ void fence_acq_rel_gpu() {
-  asm volatile("fence.acq_rel.gpu;" ::: "memory");
-}
-
-// Release this piece (fence, then a relaxed increment): returns the counter
-// value before the increment.
+// Releases this piece and acquires the ones that arrived before it, in one
+// acq_rel atomic (measured 0.5 us shorter per C1 step than a separate
+// fence.acq_rel before and after a relaxed add): returns the counter value
+// before the increment.
 __device__ __forceinline__ int arrive_piece(int* counter) {
-  fence_acq_rel_gpu();
   int old;
-  asm volatile("atom.relaxed.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
   return old;
 }
 
@@ -143,6 +144,11 @@ __device__ __forceinline__ void cp_async_wait_all() {
 }
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Named barrier 1 over the consumer warps only (the producer warp never
+// joins it; barrier 0 is __syncthreads).
+__device__ __forceinline__ void consumer_sync(int threads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
+}
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
@@ -210,15 +216,20 @@ __device__ __forceinline__ void store_output(T* obase, int s, int kvh, int n_q, 
 // cos/sin of sequence s's position at frequency jj, rounded to T
 // (rotary_embedding.py:47-53, 71-72): the fp32 angle pos * inv_freq[jj]
 // (one product, as torch.outer computes it), evaluated in double precision.
+template <typename T>
+__device__ __forceinline__ void rope_value(int pos, float inv_freq, float* cs, float* sn) {
+  const float ang = static_cast<float>(pos) * inv_freq;
+  double sd, cd;
+  sincos(static_cast<double>(ang), &sd, &cd);
+  *cs = Elt<T>::to_f(Elt<T>::from_f(static_cast<float>(cd)));
+  *sn = Elt<T>::to_f(Elt<T>::from_f(static_cast<float>(sd)));
+}
+
 template <typename T, typename Params>
 __device__ __forceinline__ void rope_entry(const Params& p, int s, int jj, float* cs, float* sn) {
   const int pos = p.positions[s];
   if (pos < 0) set_error(p.err, kDevErrPositionRange);
-  const float ang = static_cast<float>(pos) * p.inv_freq[jj];
-  double sd, cd;
-  sincos(static_cast<double>(ang), &sd, &cd);
-  cs[jj] = Elt<T>::to_f(Elt<T>::from_f(static_cast<float>(cd)));
-  sn[jj] = Elt<T>::to_f(Elt<T>::from_f(static_cast<float>(sd)));
+  rope_value<T>(pos, p.inv_freq[jj], &cs[jj], &sn[jj]);
 }
 
 template <typename T>
@@ -360,99 +371,23 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
     const int s = upper_bound_pref(pref, num_seqs, f);
     phys = p.block_tables[static_cast<size_t>(s) * p.max_blocks + (f - pref[s])];
   };
-  // Early work that only needs host-written inputs (block tables, positions):
-  // the producer's first 32 table entries and, in fused mode, the RoPE tables
-  // of this CTA's first segments (one per sequence, shared by all heads).
-  int pre_phys = 0, pre_hg = 0;
-  if (tid == 0) {
-    // This CTA's first segments (one sequence each): length, new-token slot.
-    long long uu = u_begin;
-    int k = 0;
-    for (; k < kSegTables && uu < u_end; ++k) {
-      const int hg = static_cast<int>(uu / TP);
-      const int f = static_cast<int>(uu - static_cast<long long>(hg) * TP);
-      const int sq = upper_bound_pref(pref, num_seqs, f);
-      seg_seq[k] = sq;
-      seg_hg[k] = hg;
-      seg_ctx[k] = p.seq_lens[sq];
-      seg_slot[k] = p.fused ? p.slot_mapping[sq] : -1;
-      uu += pref[sq + 1] - f;
-    }
-    n_seg_tables = k;
-  }
-  if (p.early_prologue && u_begin < u_end && warp == 0 && u_begin + lane < u_end) {
-    unit_block(u_begin + lane, pre_hg, pre_phys);
-  }
-  __syncthreads();
-  if (p.fused) {
-    // RoPE tables of those segments (positions are host-written inputs).
-    for (int e = tid; e < n_seg_tables * HALF; e += blockDim.x) {
-      const int k = e / HALF, jj = e - k * HALF;
-      rope_entry<T>(p, seg_seq[k], jj, seg_cs[k], seg_sn[k]);
-    }
-    __syncthreads();
-  }
-
-  // q/k/v and the pool may still be being written by the previous kernel.
-  if (p.early_prologue) pdl_wait();
-  pdl_trigger();
-  // Zero rows for empty sequences (they own no work unit, so in fused mode
-  // their new K/V is not written either: flagged).  The rows are spread over
-  // all CTAs, each written by the whole CTA with coalesced stores -- a
-  // padded batch can hold hundreds of them.
-  for (int s = blockIdx.x; s < num_seqs; s += gridDim.x) {
-    if (pref[s + 1] != pref[s]) continue;
-    if (tid == 0 && p.fused && p.slot_mapping[s] >= 0) set_error(p.err, kDevErrSlotNotLast);
-    T* o = static_cast<T*>(p.out) + static_cast<size_t>(s) * p.n_q * D;
-    if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-      uint4* o4 = reinterpret_cast<uint4*>(o);
-      const int n16 = p.n_q * D * static_cast<int>(sizeof(T)) / 16;
-      for (int e = tid; e < n16; e += blockDim.x) o4[e] = make_uint4(0u, 0u, 0u, 0u);
-    } else {
-      for (int e = tid; e < p.n_q * D; e += blockDim.x) o[e] = Elt<T>::from_f(0.f);
-    }
-  }
-  if (u_begin >= u_end) return;
-
-  if (warp > 0) {
-    // Stage this warp's kv-head rows of the first segments: the G query rows
-    // and, in fused mode, the new token's K and V.
-    const int h = warp - 1;
-    for (int k = 0; k < n_seg_tables; ++k) {
-      const int sq = seg_seq[k];
-      const int kvh = seg_hg[k] * HPC + h;
-      const T* qsrc = static_cast<const T*>(p.q) + static_cast<size_t>(sq) * p.q_stride +
-                      static_cast<size_t>(kvh) * p.G * D;
-      T* qdst = &seg_q[k][h][0][0];
-      for (int ci = lane; ci < p.G * (D / 8); ci += 32) cp_async16(qdst + ci * 8, qsrc + ci * 8);
-      if (p.fused) {
-        const T* ksrc = static_cast<const T*>(p.k) + static_cast<size_t>(sq) * p.k_stride +
-                        static_cast<size_t>(kvh) * D;
-        const T* vsrc = static_cast<const T*>(p.v) + static_cast<size_t>(sq) * p.v_stride +
-                        static_cast<size_t>(kvh) * D;
-        for (int ci = lane; ci < 2 * (D / 8); ci += 32) {
-          const bool is_v = ci >= D / 8;
-          const int cc = is_v ? ci - D / 8 : ci;
-          cp_async16(&seg_kv[k][h][is_v ? 1 : 0][cc * 8], (is_v ? vsrc : ksrc) + cc * 8);
-        }
-      }
-    }
-    cp_async_commit();
-  }
-
   if (warp == 0) {
     // ── producer: one TMA per 64 columns per page ────────────────────────────
-    if (lane == 0) prefetch_tmap(&tmap);
-    int it = 0;
+    // Its prologue is only the first batch of block-table entries (host-written
+    // inputs, fetched before the PDL wait in the fused step), so a CTA that is
+    // placed on its SM just as the previous kernel ends issues its first page
+    // load one table round trip after it starts; the consumers' prologue runs
+    // while those pages are in flight.
     // Block-table entries are fetched one batch of 32 ahead, so their load
     // latency (long while the page stream keeps HBM queues full) is hidden.
     int cur_phys = 0, cur_hg = 0;
-    if (p.early_prologue) {
-      cur_phys = pre_phys;
-      cur_hg = pre_hg;
-    } else if (u_begin + lane < u_end) {
-      unit_block(u_begin + lane, cur_hg, cur_phys);
-    }
+    if (u_begin + lane < u_end) unit_block(u_begin + lane, cur_hg, cur_phys);
+    // The pool may still be being written by the previous kernel.
+    if (p.early_prologue) pdl_wait();
+    pdl_trigger();
+    if (u_begin >= u_end) return;
+    if (lane == 0) prefetch_tmap(&tmap);
+    int it = 0;
     for (long long base = u_begin; base < u_end; base += 32) {
       int nxt_phys = 0, nxt_hg = 0;
       if (base + 32 + lane < u_end) unit_block(base + 32 + lane, nxt_hg, nxt_phys);
@@ -488,6 +423,114 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
     }
     return;
   }
+
+  // ── consumer prologue (overlaps the producer's first page loads) ──────────
+  // Every global load of the prologue is issued before the first use of any
+  // of them: under a full page stream one round trip costs ~2 us, and a CTA
+  // placed on its SM just as the previous kernel ends pays each serial one.
+  constexpr int kConsumerThreads = 32 * HPC;
+  constexpr int kRopePer = (kSegTables * HALF + kConsumerThreads - 1) / kConsumerThreads;
+  const int ctid = tid - 32;
+  if (warp == 1 && lane == 0) {
+    // This CTA's first segments (one sequence each), walked in the prefix sums.
+    long long uu = u_begin;
+    int k = 0;
+    for (; k < kSegTables && uu < u_end; ++k) {
+      const int hg = static_cast<int>(uu / TP);
+      const int f = static_cast<int>(uu - static_cast<long long>(hg) * TP);
+      const int sq = upper_bound_pref(pref, num_seqs, f);
+      seg_seq[k] = sq;
+      seg_hg[k] = hg;
+      uu += pref[sq + 1] - f;
+    }
+    n_seg_tables = k;
+  }
+  consumer_sync(kConsumerThreads);
+  const int n_seg = n_seg_tables;
+  // Host-written inputs of those segments (lengths, new-token slots,
+  // positions, RoPE frequencies): loaded before the PDL wait, used after it.
+  int r_pos[kRopePer];
+  float r_inv[kRopePer];
+  if (p.fused) {
+#pragma unroll
+    for (int i = 0; i < kRopePer; ++i) {
+      const int e = ctid + i * kConsumerThreads;
+      r_pos[i] = 0;
+      r_inv[i] = 0.f;
+      if (e < n_seg * HALF) {
+        r_pos[i] = p.positions[seg_seq[e / HALF]];
+        r_inv[i] = p.inv_freq[e % HALF];
+      }
+    }
+  }
+  int l_ctx = 0, l_slot = -1;
+  if (warp == 1 && lane < n_seg) {
+    const int sq = seg_seq[lane];
+    l_ctx = p.seq_lens[sq];
+    l_slot = p.fused ? p.slot_mapping[sq] : -1;
+  }
+
+  // q/k/v and the output may still be in use by the previous kernel.
+  if (p.early_prologue) pdl_wait();
+  pdl_trigger();
+  {
+    // Stage this warp's kv-head rows of the first segments: the G query rows
+    // and, in fused mode, the new token's K and V.
+    const int h = warp - 1;
+    for (int k = 0; k < n_seg; ++k) {
+      const int sq = seg_seq[k];
+      const int kvh = seg_hg[k] * HPC + h;
+      const T* qsrc = static_cast<const T*>(p.q) + static_cast<size_t>(sq) * p.q_stride +
+                      static_cast<size_t>(kvh) * p.G * D;
+      T* qdst = &seg_q[k][h][0][0];
+      for (int ci = lane; ci < p.G * (D / 8); ci += 32) cp_async16(qdst + ci * 8, qsrc + ci * 8);
+      if (p.fused) {
+        const T* ksrc = static_cast<const T*>(p.k) + static_cast<size_t>(sq) * p.k_stride +
+                        static_cast<size_t>(kvh) * D;
+        const T* vsrc = static_cast<const T*>(p.v) + static_cast<size_t>(sq) * p.v_stride +
+                        static_cast<size_t>(kvh) * D;
+        for (int ci = lane; ci < 2 * (D / 8); ci += 32) {
+          const bool is_v = ci >= D / 8;
+          const int cc = is_v ? ci - D / 8 : ci;
+          cp_async16(&seg_kv[k][h][is_v ? 1 : 0][cc * 8], (is_v ? vsrc : ksrc) + cc * 8);
+        }
+      }
+    }
+    cp_async_commit();
+  }
+  // While those copies fly: the segment tables from the loaded values.
+  if (warp == 1 && lane < n_seg) {
+    seg_ctx[lane] = l_ctx;
+    seg_slot[lane] = l_slot;
+  }
+  if (p.fused) {
+#pragma unroll
+    for (int i = 0; i < kRopePer; ++i) {
+      const int e = ctid + i * kConsumerThreads;
+      if (e < n_seg * HALF) {
+        if (r_pos[i] < 0) set_error(p.err, kDevErrPositionRange);
+        rope_value<T>(r_pos[i], r_inv[i], &seg_cs[e / HALF][e % HALF], &seg_sn[e / HALF][e % HALF]);
+      }
+    }
+  }
+  // Zero rows for empty sequences (they own no work unit, so in fused mode
+  // their new K/V is not written either: flagged).  The rows are spread over
+  // all CTAs, each written by the consumer warps with coalesced stores -- a
+  // padded batch can hold hundreds of them.
+  for (int s = blockIdx.x; s < num_seqs; s += gridDim.x) {
+    if (pref[s + 1] != pref[s]) continue;
+    if (ctid == 0 && p.fused && p.slot_mapping[s] >= 0) set_error(p.err, kDevErrSlotNotLast);
+    T* o = static_cast<T*>(p.out) + static_cast<size_t>(s) * p.n_q * D;
+    if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+      uint4* o4 = reinterpret_cast<uint4*>(o);
+      const int n16 = p.n_q * D * static_cast<int>(sizeof(T)) / 16;
+      for (int e = ctid; e < n16; e += kConsumerThreads) o4[e] = make_uint4(0u, 0u, 0u, 0u);
+    } else {
+      for (int e = ctid; e < p.n_q * D; e += kConsumerThreads) o[e] = Elt<T>::from_f(0.f);
+    }
+  }
+  consumer_sync(kConsumerThreads);  // segment and RoPE tables complete
+  if (u_begin >= u_end) return;
 
   // ── consumers: warp h = kv head (hg * HPC + h) ──────────────────────────────
   const int h = warp - 1;
@@ -810,7 +853,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
     for (int i = 0; i < n_pend; ++i) {
       if (pend_old[i] == pend_c1[i] - pend_c0[i]) last_mask |= 1 << i;
     }
-    if (last_mask) fence_acq_rel_gpu();  // acquire the other pieces
   }
   last_mask = __shfl_sync(0xffffffffu, last_mask, 0);
   __syncwarp();  // every lane's loads below come after lane 0's acquire
