@@ -801,7 +801,6 @@ def run_engine(args, rank, world, local_rank):
                                max_tokens_per_step=10 ** 9, mode="physical", dtype=dt, device=dev,
                                max_prefill_rows=16384)
     eng.capture_decode_graphs()  # startup work, outside the timed region
-    fused = eng._graphs is not None and eng._graphs.fused
     for p in prompts:
         eng.add_request(p, SamplingParams(temperature=0.0, max_tokens=steps + 1))
     torch.cuda.synchronize(dev)
@@ -863,10 +862,12 @@ def run_engine(args, rank, world, local_rank):
                          "kernel": "whole decode step (weights + every layer's K/V history)",
                          "alg_bytes_per_step": step_bytes},
             "clocks": clocks.summary(),
-            # Per step: the fused decode-step kernel per layer, plus (fused
-            # Llama layers) two add_rmsnorm + one silu_mul per layer and the
-            # first layer's input norm; the GEMMs are cuBLAS.
-            "gpu_launches": n_timed * (4 * nl + 1 if fused else nl),
+            # Per step: the decode-step kernel, two add_rmsnorm per layer and
+            # the first input norm, and at decode batch sizes the decode GEMMs
+            # (QKV, O, [gate|up] with SiLU * up, down, LM head); else cuBLAS
+            # GEMMs and a silu_mul per layer.
+            "gpu_launches": n_timed * (eng._graphs.own_kernels_per_step(B) if eng._graphs
+                                       else nl),
             "cpu_baseline": None,
             "cpu_baseline_note": "the reference's engine is Python on its CPU path; config 0 "
                                  "took 33 tokens/s on 8 host cores in the survey (config 2 is "

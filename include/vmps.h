@@ -227,6 +227,25 @@ int vmps_silu_mul(void* out, int64_t out_row_stride, const void* gate_up,
                   int64_t in_row_stride, int rows, int inter, int dtype, void* stream);
 
 /*
+ * Decode GEMM for the projections around the attention step at decode batch
+ * sizes (replaces the nn.Linear calls of the HF decoder layer that the
+ * reference's models/llama_adapter.py:137-207 runs: q/k/v, o, gate/up and
+ * down projections).  out[M, N] = x[M, K] . w[N, K]^T, fp32 accumulation,
+ * rounded to the 16-bit type.  With silu_mul != 0, w is the fused [gate; up]
+ * weight of 2N rows and out[M, N] = silu(x . Wg^T) * (x . Wu^T), each
+ * projection rounded first (transformers LlamaMLP).
+ * Shapes: M <= 8, N % 8 == 0, K % 64 == 0, K <= 8192; x and w 16-byte
+ * aligned, x rows a multiple of 8 elements apart; out 4-byte aligned with an
+ * even row stride.  vmps_decode_gemm_supported says whether a shape is
+ * built (1) or not (0), so a caller can fall back to its GEMM library.
+ * Launched with programmatic dependent launch: the weight stream starts
+ * before the wait on the previous kernel in the stream.
+ */
+int vmps_decode_gemm_supported(int M, int N, int K, int silu_mul);
+int vmps_decode_gemm(void* out, int64_t out_row_stride, const void* x, int64_t x_row_stride,
+                     const void* w, int M, int N, int K, int silu_mul, int dtype, void* stream);
+
+/*
  * Reads and clears the device error word of the current device (a bitwise OR
  * of index violations the kernels skipped since the last call).  Synchronises
  * `stream`.  Bits: 1 slot out of range, 2 block id out of range, 4 seq_len

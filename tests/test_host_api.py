@@ -58,6 +58,16 @@ def test_host_side_argument_checks_need_no_gpu():
     rc = lib.vmps_paged_decode_attention(None, None, None, None, 1, None, 0, 8, 2, 64, 16, 10,
                                          0.1, None, 0, 0, None)
     assert rc == 0  # empty batch: nothing to do
+    # Decode GEMM: shapes outside what is built are refused before any CUDA call.
+    assert lib.vmps_decode_gemm_supported(8, 2560, 2048, 0) == 1
+    assert lib.vmps_decode_gemm_supported(9, 2560, 2048, 0) == 0   # M <= 8
+    assert lib.vmps_decode_gemm_supported(8, 2564, 2048, 0) == 0   # N % 8
+    assert lib.vmps_decode_gemm_supported(8, 2560, 2080, 0) == 0   # K % 64
+    assert lib.vmps_decode_gemm_supported(8, 2560, 16384, 0) == 0  # K <= 8192
+    rc = lib.vmps_decode_gemm(None, 0, None, 0, None, 9, 2560, 2048, 0, 0, None)
+    assert rc == -2 and b"M=9" in lib.vmps_last_error()
+    rc = lib.vmps_add_rmsnorm(None, 0, None, 0, None, 0, None, 4, 12, 1e-5, 0, None)
+    assert rc == -1 and b"hidden=12" in lib.vmps_last_error()
 
 
 def test_kernel_wrappers_refuse_cpu_tensors():

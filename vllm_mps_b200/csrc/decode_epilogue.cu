@@ -26,11 +26,35 @@ namespace {
 
 constexpr int kNormThreads = 256;
 
+// Both kernels are launched with programmatic dependent launch: they wait for
+// the previous kernel's outputs, then at once let the next kernel launch (a
+// decode GEMM then streams its weights while this kernel runs).
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t s,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kNormThreads)
     add_rmsnorm_kernel(T* __restrict__ out, T* __restrict__ residual, const T* __restrict__ delta,
                        const T* __restrict__ weight, int hidden, int64_t out_stride,
                        int64_t res_stride, int64_t delta_stride, float eps) {
+  pdl_enter();
   const int row = blockIdx.x;
   T* r = residual + row * res_stride;
   const T* d = delta ? delta + row * delta_stride : nullptr;
@@ -82,6 +106,7 @@ __global__ void __launch_bounds__(kNormThreads)
 template <typename T>
 __global__ void silu_mul_kernel(T* __restrict__ out, const T* __restrict__ gate_up, int inter,
                                 int64_t out_stride, int64_t in_stride) {
+  pdl_enter();
   const int row = blockIdx.y;
   const int v = blockIdx.x * blockDim.x + threadIdx.x;  // 16-byte vector within the row
   if (v >= inter / 8) return;
@@ -129,18 +154,23 @@ extern "C" int vmps_add_rmsnorm(void* out, int64_t out_stride, void* residual, i
     return fail(VMPS_ERR_INVALID_ARG, "add_rmsnorm: dtype %d", dtype);
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
   if (dtype == VMPS_DTYPE_F16) {
-    add_rmsnorm_kernel<__half><<<rows, kNormThreads, 0, s>>>(
-        static_cast<__half*>(out), static_cast<__half*>(residual),
-        static_cast<const __half*>(delta), static_cast<const __half*>(weight), hidden, out_stride,
-        res_stride, delta_stride, eps);
+    e = launch_pdl(add_rmsnorm_kernel<__half>, dim3(rows), dim3(kNormThreads), s,
+                   static_cast<__half*>(out), static_cast<__half*>(residual),
+                   static_cast<const __half*>(delta), static_cast<const __half*>(weight), hidden,
+                   out_stride, res_stride, delta_stride, eps);
   } else {
-    add_rmsnorm_kernel<__nv_bfloat16><<<rows, kNormThreads, 0, s>>>(
-        static_cast<__nv_bfloat16*>(out), static_cast<__nv_bfloat16*>(residual),
-        static_cast<const __nv_bfloat16*>(delta), static_cast<const __nv_bfloat16*>(weight),
-        hidden, out_stride, res_stride, delta_stride, eps);
+    e = launch_pdl(add_rmsnorm_kernel<__nv_bfloat16>, dim3(rows), dim3(kNormThreads), s,
+                   static_cast<__nv_bfloat16*>(out), static_cast<__nv_bfloat16*>(residual),
+                   static_cast<const __nv_bfloat16*>(delta),
+                   static_cast<const __nv_bfloat16*>(weight), hidden, out_stride, res_stride,
+                   delta_stride, eps);
   }
-  return check_launch("add_rmsnorm");
+  if (e != cudaSuccess) {
+    return fail(VMPS_ERR_CUDA, "add_rmsnorm: launch failed: %s", cudaGetErrorString(e));
+  }
+  return VMPS_OK;
 }
 
 extern "C" int vmps_silu_mul(void* out, int64_t out_stride, const void* gate_up,
@@ -158,16 +188,19 @@ extern "C" int vmps_silu_mul(void* out, int64_t out_stride, const void* gate_up,
   if (rows > 65535) return fail(VMPS_ERR_UNSUPPORTED, "silu_mul: rows %d > 65535", rows);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 grid((inter / 8 + 127) / 128, rows);
+  cudaError_t e;
   if (dtype == VMPS_DTYPE_F16) {
-    silu_mul_kernel<__half><<<grid, 128, 0, s>>>(static_cast<__half*>(out),
-                                                  static_cast<const __half*>(gate_up), inter,
-                                                  out_stride, in_stride);
+    e = launch_pdl(silu_mul_kernel<__half>, grid, dim3(128), s, static_cast<__half*>(out),
+                   static_cast<const __half*>(gate_up), inter, out_stride, in_stride);
   } else if (dtype == VMPS_DTYPE_BF16) {
-    silu_mul_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(
-        static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(gate_up), inter,
-        out_stride, in_stride);
+    e = launch_pdl(silu_mul_kernel<__nv_bfloat16>, grid, dim3(128), s,
+                   static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(gate_up),
+                   inter, out_stride, in_stride);
   } else {
     return fail(VMPS_ERR_INVALID_ARG, "silu_mul: dtype %d", dtype);
   }
-  return check_launch("silu_mul");
+  if (e != cudaSuccess) {
+    return fail(VMPS_ERR_CUDA, "silu_mul: launch failed: %s", cudaGetErrorString(e));
+  }
+  return VMPS_OK;
 }

@@ -13,7 +13,11 @@ For Llama-family layers (RMSNorm, bias-free SiLU-gated MLP) the replayed
 forward is 8 kernels per layer: the QKV GEMM, the fused decode-step kernel,
 the O GEMM, residual add + RMSNorm (``kernels.add_rmsnorm``), one [gate|up]
 GEMM (the two weights are re-pointed as views into one buffer), SiLU * up
-(``kernels.silu_mul``), the down GEMM, and residual add + the next RMSNorm --
+(``kernels.silu_mul``), the down GEMM, and residual add + the next RMSNorm.
+At decode batch sizes (buckets up to 8) the GEMMs are the decode GEMM kernel
+(``kernels.decode_gemm``: weight streaming, SiLU * up fused into the
+[gate|up] GEMM, so 7 kernels per layer), all chained with programmatic
+dependent launch; larger buckets use cuBLAS.  These are
 the ops of transformers' LlamaDecoderLayer / LlamaRMSNorm / LlamaMLP with
 their rounding points, minus the model-level work a decode step does not use
 (masks and rotary tables: RoPE runs inside the decode kernel).  Other models
@@ -99,6 +103,26 @@ class DecodeGraphRunner:
         """Whether the replayed step uses the fused element-wise kernels."""
         return self._gate_up is not None
 
+    def own_kernels_per_step(self, batch: int) -> int:
+        """How many of this library's kernels one replayed step of ``batch`` launches."""
+        from vllm_mps_b200 import kernels as K
+
+        m = self.adapter.hf_model
+        nl = len(m.model.layers)
+        if self._gate_up is None:
+            return nl  # the decode-step kernel; the rest is HF modules
+        Bb = self.bucket(batch) or batch
+        d = self.adapter.model_config.d_model
+        a0 = m.model.layers[0].self_attn
+        n = nl + 2 * nl + 1  # decode step; residual + RMSNorm twice a layer, plus the first
+        n += nl * (K.decode_gemm_supported(Bb, a0._w_qkv.shape[0], d)
+                   + K.decode_gemm_supported(Bb, d, a0.W_O.in_features))
+        n += nl  # the [gate|up] decode GEMM with SiLU * up, or silu_mul after cuBLAS
+        down = m.model.layers[0].mlp.down_proj
+        n += nl * K.decode_gemm_supported(Bb, down.out_features, down.in_features)
+        n += K.decode_gemm_supported(Bb, m.lm_head.out_features, d)
+        return n
+
     @staticmethod
     def bucket(batch: int) -> int | None:
         for b in BUCKETS:
@@ -128,23 +152,35 @@ class DecodeGraphRunner:
         """Per layer: QKV GEMM, decode-step kernel, O GEMM, add+RMSNorm,
         [gate|up] GEMM, SiLU*up, down GEMM, add+RMSNorm (the next layer's input
         norm, or the final norm) -- 8 kernels."""
-        from vllm_mps_b200.kernels import add_rmsnorm, silu_mul
+        from vllm_mps_b200 import kernels as K
+        from vllm_mps_b200.layers.paged_attention_layer import PagedAttentionLayer
 
+        project = PagedAttentionLayer.project
         m = self.adapter.hf_model
         layers = m.model.layers
         res = m.model.embed_tokens(st.tokens)  # (Bb, d): the residual stream
         h = torch.empty_like(res)
+        Bb, d = res.shape
         first = layers[0].input_layernorm
-        add_rmsnorm(res, first.weight, first.variance_epsilon, out=h)
+        K.add_rmsnorm(res, first.weight, first.variance_epsilon, out=h)
         for i, layer in enumerate(layers):
             attn = layer.self_attn._attend(h.unsqueeze(1), st.meta)
             post = layer.post_attention_layernorm
-            add_rmsnorm(res, post.weight, post.variance_epsilon, delta=attn.view_as(res), out=h)
-            act = silu_mul(torch.matmul(h, self._gate_up[i].t()))
-            mlp_out = layer.mlp.down_proj(act)
+            K.add_rmsnorm(res, post.weight, post.variance_epsilon, delta=attn.view_as(res), out=h)
+            gu = self._gate_up[i]
+            if K.decode_gemm_supported(Bb, gu.shape[0] // 2, d, True):
+                act = K.decode_gemm(h, gu, silu_mul=True)  # [gate|up] GEMM + SiLU * up
+            else:
+                act = K.silu_mul(torch.matmul(h, gu.t()))
+            down = layer.mlp.down_proj
+            mlp_out = project(act, down.weight) if down.bias is None else down(act)
             nxt = layers[i + 1].input_layernorm if i + 1 < len(layers) else m.model.norm
-            add_rmsnorm(res, nxt.weight, nxt.variance_epsilon, delta=mlp_out, out=h)
-        st.logits.copy_(m.lm_head(h))
+            K.add_rmsnorm(res, nxt.weight, nxt.variance_epsilon, delta=mlp_out, out=h)
+        head = m.lm_head
+        if head.bias is None and K.decode_gemm_supported(Bb, head.out_features, d):
+            K.decode_gemm(h, head.weight, out=st.logits)
+        else:
+            st.logits.copy_(head(h))
 
     def _static(self, Bb: int):
         """Static buffers of a bucket: [tables Bb x W | lengths | positions | slots | tokens]."""

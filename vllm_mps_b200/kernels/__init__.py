@@ -53,6 +53,8 @@ EXPORTED_SYMBOLS = (
     "vmps_paged_prefill_attention",
     "vmps_add_rmsnorm",
     "vmps_silu_mul",
+    "vmps_decode_gemm_supported",
+    "vmps_decode_gemm",
     "vmps_debug_error_word",
 )
 
@@ -101,6 +103,10 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.vmps_add_rmsnorm.argtypes = [vp, i64, vp, i64, vp, i64, vp, i32, i32, f32, i32, vp]
         lib.vmps_silu_mul.restype = i32
         lib.vmps_silu_mul.argtypes = [vp, i64, vp, i64, i32, i32, i32, vp]
+        lib.vmps_decode_gemm_supported.restype = i32
+        lib.vmps_decode_gemm_supported.argtypes = [i32, i32, i32, i32]
+        lib.vmps_decode_gemm.restype = i32
+        lib.vmps_decode_gemm.argtypes = [vp, i64, vp, i64, vp, i32, i32, i32, i32, i32, vp]
         lib.vmps_debug_error_word.restype = i32
         lib.vmps_debug_error_word.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
         if path is None:
@@ -474,6 +480,47 @@ def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Te
         rc = lib.vmps_silu_mul(_ptr(out), _row_stride(out, inter, "out"), _ptr(gate_up), ins,
                                rows, inter, dtype_code(gate_up.dtype), _stream(dev))
     _check(rc, "silu_mul")
+    return out
+
+
+def decode_gemm_supported(m: int, n: int, k: int, silu_mul: bool = False) -> bool:
+    """Whether ``decode_gemm`` is built for this shape (M <= 8, N % 8, K % 64, K <= 8192)."""
+    return bool(load_library().vmps_decode_gemm_supported(int(m), int(n), int(k), int(silu_mul)))
+
+
+def decode_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
+                silu_mul: bool = False) -> torch.Tensor:
+    """``x @ w.T`` for decode batch sizes (M <= 8), weight-streaming on HBM.
+
+    The projections of a decoder layer at decode time (nn.Linear without
+    bias, as transformers' Llama layers call them).  ``x``: (M, K) with unit
+    inner stride; ``w``: contiguous (N, K).  With ``silu_mul`` the weight is
+    the fused [gate; up] matrix of 2I rows and the result is
+    ``silu(x @ Wg.T) * (x @ Wu.T)`` of shape (M, I), each projection rounded
+    to the dtype first (LlamaMLP).  Returns ``out``.
+    """
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be 2-D (M, K) with unit inner stride")
+    if w.dim() != 2 or not w.is_contiguous():
+        raise ValueError("w must be a contiguous (N, K) matrix")
+    M, K = x.shape
+    if w.shape[1] != K:
+        raise ValueError(f"x has K={K}, w has K={w.shape[1]}")
+    if w.dtype != x.dtype:
+        raise TypeError(f"w dtype {w.dtype} != x dtype {x.dtype}")
+    if silu_mul and w.shape[0] % 2:
+        raise ValueError("silu_mul needs a [gate; up] weight with an even row count")
+    N = w.shape[0] // 2 if silu_mul else w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    elif out.shape != (M, N) or out.dtype != x.dtype or out.stride(1) != 1:
+        raise ValueError(f"out must be ({M}, {N}) of x's dtype with unit inner stride")
+    dev = _require_cuda(x, w, out)
+    lib = load_library()
+    with torch.cuda.device(dev):
+        rc = lib.vmps_decode_gemm(_ptr(out), out.stride(0), _ptr(x), x.stride(0), _ptr(w), M, N, K,
+                                  int(bool(silu_mul)), dtype_code(x.dtype), _stream(dev))
+    _check(rc, "decode_gemm")
     return out
 
 

@@ -100,13 +100,26 @@ class PagedAttentionLayer(nn.Module):
             self._workspace = DecodeWorkspace()
         return self._workspace
 
+    @staticmethod
+    def project(x2d: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """``x2d @ w.T``: the decode GEMM kernel at decode batch sizes (M <= 8,
+        weight streaming, chained to its neighbours with programmatic dependent
+        launch), cuBLAS for everything else."""
+        from vllm_mps_b200 import kernels as K
+
+        if (x2d.is_cuda and x2d.stride(1) == 1 and x2d.stride(0) % 8 == 0
+                and x2d.data_ptr() % 16 == 0 and w.is_contiguous() and w.data_ptr() % 16 == 0
+                and K.decode_gemm_supported(x2d.shape[0], w.shape[0], w.shape[1])):
+            return K.decode_gemm(x2d, w)
+        return torch.matmul(x2d, w.t())
+
     def _attend(self, hidden_states: torch.Tensor, meta) -> torch.Tensor:
         """Fused QKV GEMM -> one decode-step kernel -> W_O, for (B, 1, d_model)."""
         from vllm_mps_b200.kernels import paged_decode_step
 
         B = hidden_states.shape[0]
         n_q, n_kv, D = self.n_heads, self.n_kv_heads, self.d_k
-        qkv = torch.matmul(hidden_states.reshape(B, self.d_model), self._w_qkv.t())
+        qkv = self.project(hidden_states.reshape(B, self.d_model), self._w_qkv)
         q = qkv[:, : n_q * D].view(B, n_q, D)
         k = qkv[:, n_q * D: (n_q + n_kv) * D]
         v = qkv[:, (n_q + n_kv) * D:]
@@ -114,6 +127,8 @@ class PagedAttentionLayer(nn.Module):
                                 self.rotary_emb.inv_freq, self._pool(), meta.bt_tensor,
                                 meta.sl_tensor, scale=1.0 / math.sqrt(D),
                                 workspace=self._workspace_buf())
+        if self.W_O.bias is None:
+            return self.project(out.view(B, n_q * D), self.W_O.weight).view(B, 1, -1)
         return self.W_O(out.view(B, 1, n_q * D))
 
     def _prefill_rows(self, hidden_states: torch.Tensor, meta) -> torch.Tensor:
