@@ -980,13 +980,179 @@ def run_c4(args, rank, world, local_rank):
     return 0
 
 
+# ── decode GEMM (the engine's projections at decode batch sizes) ───────────
+
+GEMM_SHAPES = (
+    # name, output features, K, gated ([gate; up] weight of 2N rows + SiLU * up)
+    ("qkv", 2560, 2048, False),
+    ("o", 2048, 2048, False),
+    ("gate_up", 5632, 2048, True),
+    ("down", 2048, 5632, False),
+    ("lm_head", 32000, 2048, False),
+)
+
+
+def run_gemm(args, rank, world, local_rank):
+    """Decode GEMM on the TinyLlama decode projections (M = 8, fp16).
+
+    A step is one pass of the five projections of a config-0 decode step
+    (QKV, O, [gate; up] with SiLU * up, down, LM head) through
+    ``kernels.decode_gemm``; four weight sets (876 MB) rotate so inputs are
+    larger than L2.  ``value`` is weight GB/s over the step; each projection
+    is also timed alone (40 launches in a CUDA graph) next to cuBLAS
+    (``F.linear``, plus ``silu_mul`` for the gated one).
+    """
+    import torch
+    import torch.nn.functional as F
+
+    from vllm_mps_b200 import kernels as K
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    M, R, dt = 8, 4, torch.float16
+    g = torch.Generator(device=dev).manual_seed(5)
+    W = {n: [(torch.randn((2 * N if gated else N), Kd, generator=g, device=dev) / Kd ** 0.5).to(dt)
+             for _ in range(R)] for n, N, Kd, gated in GEMM_SHAPES}
+    X = {Kd: torch.randn(M, Kd, generator=g, device=dev).to(dt) for Kd in (2048, 5632)}
+    OUT = {n: torch.empty(M, N, device=dev, dtype=dt) for n, N, Kd, gated in GEMM_SHAPES}
+    weight_bytes = sum(W[n][0].numel() * 2 for n, *_ in GEMM_SHAPES)
+
+    def step(r):
+        for n, N, Kd, gated in GEMM_SHAPES:
+            K.decode_gemm(X[Kd], W[n][r], out=OUT[n], silu_mul=gated)
+
+    def capture(fns):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for f in fns:
+                f()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for f in fns:
+                f()
+        return gr
+
+    def timed(gr, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) * 1e-3
+
+    g_steps = capture([lambda r=r: step(r) for r in range(R)])
+    for _ in range(max(1, args.warmup // R)):
+        g_steps.replay()
+    reps = max(1, args.steps // R)
+    with ClockSampler(dev.index or 0) as clocks:
+        t = timed(g_steps, reps)
+    n_steps = reps * R
+    t_step = t / n_steps
+
+    per = {}
+    for n, N, Kd, gated in GEMM_SHAPES:
+        it = [0]
+
+        def ours(n=n, Kd=Kd, gated=gated):
+            it[0] = (it[0] + 1) % R
+            K.decode_gemm(X[Kd], W[n][it[0]], out=OUT[n], silu_mul=gated)
+
+        def cublas(n=n, Kd=Kd, gated=gated):
+            it[0] = (it[0] + 1) % R
+            y = F.linear(X[Kd], W[n][it[0]])
+            if gated:
+                K.silu_mul(y, out=OUT[n])
+
+        a, b = capture([ours] * 40), capture([cublas] * 40)
+        timed(a, 2), timed(b, 2)
+        ta, tb = timed(a, 5) / 200, timed(b, 5) / 200
+        per[n] = {"us": round(ta * 1e6, 2), "gb_s": round(W[n][0].numel() * 2 / ta / 1e9, 1),
+                  "cublas_us": round(tb * 1e6, 2)}
+
+    # End to end: X from pinned host memory in, the LM-head logits back, per step.
+    xh = {Kd: X[Kd].cpu().pin_memory() for Kd in X}
+    oh = torch.empty(M, 32000, dtype=dt).pin_memory()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = min(n_steps, 200)
+    e0.record()
+    for i in range(n_e2e):
+        for Kd in X:
+            X[Kd].copy_(xh[Kd], non_blocking=True)
+        step(i % R)
+        oh.copy_(OUT["lm_head"], non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t_e2e = e0.elapsed_time(e1) * 1e-3 / n_e2e
+    if K.error_word(dev):
+        raise RuntimeError("device error word set during the decode-GEMM run")
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        lm = per["lm_head"]
+        traffic = None
+        try:
+            for line in open(os.path.join(ROOT, "profiles", "decode_gemm_tinyllama.md")):
+                if line.startswith("traffic_bytes_per_launch:"):
+                    traffic = int(line.split(":")[1])
+        except OSError:
+            pass
+        # CPU baseline: the same five projections as torch float32 matmuls on
+        # the host cores (the reference runs them as nn.Linear on its CPU path).
+        torch.set_num_threads(os.cpu_count() or 1)
+        wc = {n: W[n][0].float().cpu() for n, *_ in GEMM_SHAPES}
+        xc = {Kd: X[Kd].float().cpu() for Kd in X}
+        t0, n_cpu = time.perf_counter(), 0
+        while time.perf_counter() - t0 < 5.0 and n_cpu < 50:
+            for n, N, Kd, gated in GEMM_SHAPES:
+                y = xc[Kd] @ wc[n].t()
+                if gated:
+                    y = F.silu(y[:, :N]) * y[:, N:]
+            n_cpu += 1
+        t_cpu = (time.perf_counter() - t0) / n_cpu
+        line = {
+            "metric": "decode-GEMM weight stream", "value": weight_bytes / t_step / 1e9,
+            "unit": "GB/s", "n_gpus": 1, "steps": n_steps, "warmup": args.warmup,
+            "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded N(0,1)/sqrt(K) weights, N(0,1) activations)",
+            "config": {"workload": "TinyLlama decode projections at M=8 (QKV, O, [gate;up] + "
+                                   "SiLU*up, down, LM head) through kernels.decode_gemm",
+                       "global_batch": M, "weight_bytes_per_step": weight_bytes,
+                       "l2": "inputs larger than L2: 4 weight sets (876 MB) rotated",
+                       "per_projection": per},
+            "e2e": {"value": weight_bytes / t_e2e / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": sum(x.numel() * 2 for x in X.values()),
+                    "d2h_bytes_per_step": oh.numel() * 2,
+                    "api": "kernels.decode_gemm; per step X copied in from pinned memory and "
+                           "the LM-head output copied back, not overlapped"},
+            "roofline": {"bound": "hbm", "achieved": lm["gb_s"], "peak": peak, "unit": "GB/s",
+                         "frac": lm["gb_s"] / peak, "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": "decode_gemm_kernel (LM head, 32000 x 2048, M=8)",
+                         "kernel_us": lm["us"], "alg_bytes_per_launch": 32000 * 2048 * 2},
+            "clocks": clocks.summary(),
+            "gpu_launches": n_steps * len(GEMM_SHAPES),
+            "cpu_baseline": {"value": weight_bytes / t_cpu / 1e9, "unit": "GB/s",
+                             "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"{n_cpu} passes of the five projections, torch float32 "
+                                       "matmul on the host cores"},
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PREFILL) + sorted(ENGINE) + ["c4"],
+    ap.add_argument("--config",
+                    choices=sorted(CONFIGS) + sorted(PREFILL) + sorted(ENGINE) + ["c4", "gemm"],
                     default="c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -998,7 +1164,7 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference" and cfg is not None:
         return run_reference(args, cfg, rank, world)
-    if args.impl == "reference" and (args.config in ENGINE or args.config == "c4"):
+    if args.impl == "reference" and (args.config in ENGINE or args.config in ("c4", "gemm")):
         if rank == 0:
             print(json.dumps({"impl": "reference", "unavailable":
                               "the reference engine is Python on its CPU path and does not travel "
@@ -1016,6 +1182,8 @@ def main():
     try:
         if args.config == "c4":
             return run_c4(args, rank, world, local_rank)
+        if args.config == "gemm":
+            return run_gemm(args, rank, world, local_rank)
         if args.config in ENGINE:
             return run_engine(args, rank, world, local_rank)
         if cfg is None:
