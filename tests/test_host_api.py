@@ -272,6 +272,18 @@ def test_decode_graph_fused_layer_eligibility():
     assert fused[1].shape == (256, 64) and torch.equal(fused[1][:128], w_gate)
     # The module weights are views of the fused buffer: one copy of the weights.
     assert model.model.layers[1].mlp.up_proj.weight.data_ptr() == fused[1][128:].data_ptr()
+    # Kernels a replayed step launches: at decode batch sizes every projection
+    # is a decode GEMM (SiLU * up fused), so 7 per layer plus the first norm
+    # and the LM head; here the 100-row vocabulary is not a multiple of 8, so
+    # the LM head stays on cuBLAS.
+    r._gate_up = fused
+    a0 = model.model.layers[0].self_attn
+    a0._w_qkv = torch.zeros(128, 64)
+    a0.W_O = nn.Linear(64, 64, bias=False)
+    model.model.layers[1].self_attn._w_qkv = a0._w_qkv
+    model.model.layers[1].self_attn.W_O = a0.W_O
+    r.adapter.model_config.d_model = 64
+    assert r.own_kernels_per_step(8) == 7 * 2 + 1
     model.model.layers[0].mlp.act_fn = nn.GELU()
     assert not r._llama_layers()
 
