@@ -4,6 +4,8 @@ from __future__ import annotations
 
 import logging
 
+import numpy as np
+
 from vllm_mps_b200.config import BLOCK_SIZE
 from vllm_mps_b200.core.block import PhysicalBlock
 from vllm_mps_b200.core.block_allocator import BlockAllocator
@@ -20,11 +22,22 @@ class BlockTable:
         self._allocator = allocator
         self._blocks: list[PhysicalBlock] = []
         self._num_tokens = 0
+        # The block ids as an int32 array, kept current by append_slot so a
+        # decode step can copy a table without walking its blocks in Python;
+        # rebuilt after replace_blocks (swap, fork).
+        self._ids = np.empty(16, np.int32)
+        self._ids_valid = True
 
     def append_slot(self) -> PhysicalBlock:
         """Add one token slot, allocating a block when the last one is full (:45-64)."""
         if not self._blocks or self._blocks[-1].is_full:
-            self._blocks.append(self._allocator.allocate())
+            block = self._allocator.allocate()
+            self._blocks.append(block)
+            if self._ids_valid:
+                n = len(self._blocks)
+                if n > len(self._ids):
+                    self._ids = np.concatenate([self._ids, np.empty(len(self._ids), np.int32)])
+                self._ids[n - 1] = block.block_id
         last = self._blocks[-1]
         last.add_tokens(1)
         self._num_tokens += 1
@@ -35,6 +48,7 @@ class BlockTable:
         for block in self._blocks:
             self._allocator.free(block)
         self._blocks.clear()
+        self._ids_valid = True
         self._num_tokens = 0
         logger.info("BlockTable [seq=%d]: freed %d blocks", self.seq_id, n)
 
@@ -47,6 +61,22 @@ class BlockTable:
     def get_all_physical_block_ids(self) -> list[int]:
         """Ordered physical block ids (what the attention kernel reads)."""
         return [b.block_id for b in self._blocks]
+
+    def replace_blocks(self, blocks: list[PhysicalBlock]) -> None:
+        """Point the table at another list of blocks (swap, fork)."""
+        self._blocks = blocks
+        self._ids_valid = False
+
+    def block_ids(self) -> np.ndarray:
+        """The ordered physical block ids as an int32 array (read-only view)."""
+        n = len(self._blocks)
+        if not self._ids_valid:
+            self._ids = np.empty(max(16, n), np.int32)
+            self._ids[:n] = [b.block_id for b in self._blocks]
+            self._ids_valid = True
+        view = self._ids[:n]
+        view.flags.writeable = False
+        return view
 
     def get_last_block(self) -> PhysicalBlock:
         if not self._blocks:

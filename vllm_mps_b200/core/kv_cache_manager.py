@@ -79,7 +79,7 @@ class KVCacheManager:
         child = BlockTable(child_seq_id, self._gpu_allocator)
         for block in parent._blocks:
             self._gpu_allocator.fork(block)
-            child._blocks.append(block)
+        child.replace_blocks(list(parent._blocks))
         child._num_tokens = parent._num_tokens
         self._block_tables[child_seq_id] = child
         logger.info("KVCacheManager: forked seq=%d -> seq=%d, %d blocks shared",
@@ -101,7 +101,7 @@ class KVCacheManager:
             new_blocks.append(cpu_block)
         if self.swap_space is not None and pairs:
             self.swap_space.copy_out([g for g, _ in pairs], [c for _, c in pairs])
-        table._blocks = new_blocks
+        table.replace_blocks(new_blocks)
         table._allocator = self._cpu_allocator
         logger.info("KVCacheManager: swapped out seq=%d, %d blocks to CPU", seq_id, len(pairs))
 
@@ -119,11 +119,17 @@ class KVCacheManager:
             new_blocks.append(gpu_block)
         if self.swap_space is not None and pairs:
             self.swap_space.copy_in([c for c, _ in pairs], [g for _, g in pairs])
-        table._blocks = new_blocks
+        table.replace_blocks(new_blocks)
         table._allocator = self._gpu_allocator
         logger.info("KVCacheManager: swapped in seq=%d, %d blocks to GPU", seq_id, len(pairs))
 
     # ── introspection ────────────────────────────────────────────────────────
+
+    def get_block_ids(self, seq_id: int):
+        """``get_block_table`` as a read-only int32 numpy array (no per-call list)."""
+        if seq_id not in self._block_tables:
+            raise KeyError(f"KVCacheManager: seq_id {seq_id} not found.")
+        return self._block_tables[seq_id].block_ids()
 
     def get_block_table(self, seq_id: int) -> list[int]:
         """Ordered physical block ids of ``seq_id`` (:252-265)."""

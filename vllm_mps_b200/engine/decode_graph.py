@@ -205,7 +205,7 @@ class DecodeGraphRunner:
         h[:] = 0
         bt = h[:Bb * W].reshape(Bb, W)
         for i, sid in enumerate(seq_ids):
-            t = self.kv.get_block_table(sid)
+            t = self.kv.get_block_ids(sid)
             bt[i, :len(t)] = t
         o = Bb * W
         pos = np.asarray(positions, dtype=np.int64)
@@ -241,7 +241,7 @@ class DecodeGraphRunner:
     def can_run(self, seq_ids) -> bool:
         if self.bucket(len(seq_ids)) is None:
             return False
-        return all(len(self.kv.get_block_table(s)) <= self.max_blocks for s in seq_ids)
+        return all(len(self.kv.get_block_ids(s)) <= self.max_blocks for s in seq_ids)
 
     def run(self, token_ids, seq_ids, positions, seq_lens) -> torch.Tensor:
         """Logits ``(B, vocab)`` of one decode step (a view of the bucket's static buffer)."""

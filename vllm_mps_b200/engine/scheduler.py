@@ -68,6 +68,15 @@ class Scheduler:
         reserve = int(math.floor(total * (1.0 - self.preempt_watermark)))
         return math.ceil(need_tokens / kv.block_size) <= kv.get_num_free_gpu_blocks() - reserve
 
+    def _free_beyond_reserve(self) -> int:
+        """Free GPU blocks minus the watermark's reserve (the count _fits compares with)."""
+        kv = self.kv_cache_manager
+        free = kv.get_num_free_gpu_blocks()
+        if self.preempt_watermark is None:
+            return free
+        total = kv._gpu_allocator.total_blocks
+        return free - int(math.floor(total * (1.0 - self.preempt_watermark)))
+
     def schedule(self) -> SchedulerOutput:
         scheduled: list[SequenceGroup] = []
         preempted: list[SequenceGroup] = []
@@ -117,11 +126,15 @@ class Scheduler:
             n_tokens += total
             admitted.append(group)
 
-        # 3. keep or preempt the groups that were already running (:163-187)
+        # 3. keep or preempt the groups that were already running (:163-187).
+        # Every check asks for one token against the same free-block count
+        # (nothing is allocated until step 4), so when at least one block is
+        # free beyond the reserve every group fits and the checks are skipped.
         picked = {id(g) for g in scheduled}
+        all_fit = self._free_beyond_reserve() >= 1
         for group in [g for g in self._running if id(g) not in picked]:
             seqs = group.get_seqs(SequenceStatus.RUNNING)
-            if all(self._fits(s.seq_id, 1) for s in seqs):
+            if all_fit or all(self._fits(s.seq_id, 1) for s in seqs):
                 scheduled.append(group)
                 n_seqs += len(seqs)
                 n_tokens += sum(s.get_total_len() for s in seqs)
