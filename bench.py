@@ -1165,10 +1165,13 @@ def main():
     if args.impl == "reference" and cfg is not None:
         return run_reference(args, cfg, rank, world)
     if args.impl == "reference" and (args.config in ENGINE or args.config in ("c4", "gemm")):
+        why = ("the reference engine is Python on its CPU path and does not travel to the GPU box; "
+               "see the c1/c3/prefill reference lines")
+        if args.config == "gemm":
+            why = ("the reference runs these projections as nn.Linear inside its CPU engine; the "
+                   "ours-line's cpu_baseline times them as torch float32 matmuls on the host cores")
         if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable":
-                              "the reference engine is Python on its CPU path and does not travel "
-                              "to the GPU box; see the c1/c3/prefill reference lines"}))
+            print(json.dumps({"impl": "reference", "unavailable": why}))
         return 0
     if args.impl == "reference":
         return run_prefill(args, rank, world, local_rank)
