@@ -23,6 +23,7 @@ from __future__ import annotations
 import heapq
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 
 
@@ -134,28 +135,29 @@ class ShardedEngine:
         if len(produced) > self.capacity:
             raise RuntimeError(f"rank {self.rank}: {len(produced)} sequences in one step "
                                f"exceed the record capacity {self.capacity}")
-        rec = torch.full((self._rec,), -1, dtype=torch.int32)
+        # The record is built and read as numpy arrays: element-wise torch
+        # indexing cost ~3 ms per step at 256 sequences per rank.
+        rec = np.full(self._rec, -1, dtype=np.int32)
         rec[0] = 0 if self.engine.is_finished() else 1
-        for j, out in enumerate(produced):
-            rec[1 + 3 * j] = self._local_to_global[out.request_id]
-            rec[2 + 3 * j] = out.token_ids[-1]
-            rec[3 + 3 * j] = int(out.finished)
-        self._send.copy_(rec, non_blocking=False)
+        n = len(produced)
+        if n:
+            rec[1:1 + 3 * n:3] = [self._local_to_global[o.request_id] for o in produced]
+            rec[2:2 + 3 * n:3] = [o.token_ids[-1] for o in produced]
+            rec[3:3 + 3 * n:3] = [int(o.finished) for o in produced]
+        self._send.copy_(torch.from_numpy(rec), non_blocking=False)
         dist.all_gather_into_tensor(self._recv, self._send, group=self.group)
-        allrec = self._recv.view(self.world, self._rec).cpu()
-        more = False
+        allrec = self._recv.view(self.world, self._rec).cpu().numpy()
+        more = bool((allrec[:, 0] > 0).any())
         for r in range(self.world):
-            row = allrec[r]
-            more |= bool(row[0] > 0)
-            for j in range(self.capacity):
-                gid = int(row[1 + 3 * j])
-                if gid < 0:
-                    break
+            body = allrec[r, 1:1 + 3 * self.capacity].reshape(self.capacity, 3)
+            neg = np.flatnonzero(body[:, 0] < 0)
+            n_r = int(neg[0]) if neg.size else self.capacity
+            for gid, tok, fin in body[:n_r].tolist():
                 o = self.outputs[gid]
                 if o.rank != r:
                     raise RuntimeError(f"request {gid} reported by rank {r}, owned by {o.rank}")
-                o.token_ids.append(int(row[2 + 3 * j]))
-                o.finished = bool(row[3 + 3 * j])
+                o.token_ids.append(tok)
+                o.finished = bool(fin)
         self.steps += 1
         return more
 
