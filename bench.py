@@ -882,7 +882,7 @@ def run_engine(args, rank, world, local_rank):
 
 C4 = ("Config 4: TinyLlama shape (config 0 model), 1024 requests, prompts "
       "clip(round(lognormal(6,1)),16,4096), outputs U[16,512], FCFS, preemption when the pool "
-      "is 90% full, sequence-sharded (one engine per GPU, NCCL token gather)")
+      "is 90% full, sequence-sharded (one engine per GPU, NCCL token gather every 16 steps)")
 
 
 def run_c4(args, rank, world, local_rank):
@@ -932,7 +932,7 @@ def run_c4(args, rank, world, local_rank):
     with ClockSampler(dev.index or 0) as clocks:
         e0.record()
         if dist is not None:
-            sharded = ShardedEngine(eng)
+            sharded = ShardedEngine(eng, gather_every=16)
             sharded.add_requests(prompts, params)
             outs = sharded.run()
             done = sum(len(o.token_ids) for o in outs.values())

@@ -114,10 +114,10 @@ def _init(rank, world, path, timeout_s=20):
                             timeout=datetime.timedelta(seconds=timeout_s))
 
 
-def _gather_worker(rank, world, path, result_dir):
+def _gather_worker(rank, world, path, result_dir, every=1):
     _init(rank, world, path)
     prompts, params = _workload()
-    eng = ShardedEngine(FakeEngine(batch=3))
+    eng = ShardedEngine(FakeEngine(batch=3), gather_every=every)
     owner = eng.add_requests(prompts, params)
     outs = eng.run()
     res = {"owner": owner, "steps": eng.steps,
@@ -134,14 +134,17 @@ def _spawn(fn, world, *args):
     return d
 
 
-@pytest.mark.parametrize("world", [1, 2])
-def test_gather_assembles_every_request_on_every_rank(world):
-    d = _spawn(_gather_worker, world)
+@pytest.mark.parametrize("world,every", [(1, 1), (2, 1), (2, 3)])
+def test_gather_assembles_every_request_on_every_rank(world, every):
+    """Every rank assembles every request's tokens, in order, whether the ranks
+    gather after every step or buffer ``every`` steps between gathers."""
+    d = _spawn(_gather_worker, world, every)
     res = [torch.load(os.path.join(d, f"r{r}.pt")) for r in range(world)]
     prompts, params = _workload()
     for r in range(world):
         assert res[r]["owner"] == res[0]["owner"]
         assert res[r]["steps"] == res[0]["steps"]  # same collective count on every rank
+        assert res[r]["steps"] % every == 0        # the run ends at a gather
         for g, p in enumerate(prompts):
             want = [expected_token(p, t) for t in range(params[g].max_tokens)]
             assert res[r]["tokens"][g] == want, (r, g)

@@ -59,7 +59,7 @@ class ShardedOutput:
 
 
 class ShardedEngine:
-    """Runs one engine per rank and gathers sampled tokens every step.
+    """Runs one engine per rank and gathers sampled tokens every ``gather_every`` steps.
 
     ``engine`` is this rank's engine (anything with ``add_request(prompt,
     params) -> local id``, ``step() -> outputs with .request_id, .token_ids,
@@ -71,16 +71,26 @@ class ShardedEngine:
     running ones, so one step may schedule more than ``max_batch_size``
     (engine/scheduler.py:127-187).  A smaller explicit ``capacity`` saves
     bandwidth and is checked before every collective.
+
+    With ``gather_every`` = k > 1 each rank buffers the tokens of k local
+    steps and the ranks meet once per k steps (a record then holds
+    ``1 + 3 * capacity * k`` int32).  The ranks run in lockstep only at the
+    gathers, so a step that is long on one rank (a chunked prefill) and short
+    on another is no longer paid as the slower of the two every step.
     """
 
     def __init__(self, engine, capacity: int | None = None, group=None,
-                 device: torch.device | None = None):
+                 device: torch.device | None = None, gather_every: int = 1):
         import torch.distributed as dist
 
         self.engine = engine
         self.capacity = None if capacity is None else int(capacity)
         if self.capacity is not None and self.capacity < 1:
             raise ValueError("capacity must be >= 1")
+        if int(gather_every) < 1:
+            raise ValueError("gather_every must be >= 1")
+        self.gather_every = int(gather_every)
+        self._pending: list[tuple[int, int, int]] = []
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -101,7 +111,7 @@ class ShardedEngine:
             for r in owner:
                 counts[r] += 1
             self.capacity = max(1, max(counts))
-        self._rec = 1 + 3 * self.capacity
+        self._rec = 1 + 3 * self.capacity * self.gather_every
         self._send = torch.empty(self._rec, dtype=torch.int32, device=self.device)
         self._recv = torch.empty(self.world * self._rec, dtype=torch.int32, device=self.device)
 
@@ -125,8 +135,10 @@ class ShardedEngine:
                 self._local_to_global[local] = gid
         return owner
 
-    def step(self) -> bool:
-        """One local engine step and the token gather; False once every rank is done."""
+    def step(self, force_gather: bool = False) -> bool:
+        """One local engine step; every ``gather_every`` calls (or when forced:
+        every rank must pass the same value) the token gather.  Returns False
+        once a gather shows every rank done."""
         import torch.distributed as dist
 
         if self._send is None:
@@ -135,35 +147,40 @@ class ShardedEngine:
         if len(produced) > self.capacity:
             raise RuntimeError(f"rank {self.rank}: {len(produced)} sequences in one step "
                                f"exceed the record capacity {self.capacity}")
+        self._pending.extend((self._local_to_global[o.request_id], o.token_ids[-1],
+                              int(o.finished)) for o in produced)
+        self.steps += 1
+        if not force_gather and self.steps % self.gather_every:
+            return True
         # The record is built and read as numpy arrays: element-wise torch
         # indexing cost ~3 ms per step at 256 sequences per rank.
         rec = np.full(self._rec, -1, dtype=np.int32)
         rec[0] = 0 if self.engine.is_finished() else 1
-        n = len(produced)
+        n = len(self._pending)
         if n:
-            rec[1:1 + 3 * n:3] = [self._local_to_global[o.request_id] for o in produced]
-            rec[2:2 + 3 * n:3] = [o.token_ids[-1] for o in produced]
-            rec[3:3 + 3 * n:3] = [int(o.finished) for o in produced]
+            rec[1:1 + 3 * n] = np.asarray(self._pending, dtype=np.int32).reshape(-1)
+        self._pending.clear()
         self._send.copy_(torch.from_numpy(rec), non_blocking=False)
         dist.all_gather_into_tensor(self._recv, self._send, group=self.group)
         allrec = self._recv.view(self.world, self._rec).cpu().numpy()
         more = bool((allrec[:, 0] > 0).any())
+        slots = (self._rec - 1) // 3
         for r in range(self.world):
-            body = allrec[r, 1:1 + 3 * self.capacity].reshape(self.capacity, 3)
+            body = allrec[r, 1:1 + 3 * slots].reshape(slots, 3)
             neg = np.flatnonzero(body[:, 0] < 0)
-            n_r = int(neg[0]) if neg.size else self.capacity
+            n_r = int(neg[0]) if neg.size else slots
             for gid, tok, fin in body[:n_r].tolist():
                 o = self.outputs[gid]
                 if o.rank != r:
                     raise RuntimeError(f"request {gid} reported by rank {r}, owned by {o.rank}")
                 o.token_ids.append(tok)
                 o.finished = bool(fin)
-        self.steps += 1
         return more
 
     def run(self, max_steps: int | None = None) -> dict[int, ShardedOutput]:
         """Step until every rank's shard is finished (or ``max_steps``)."""
         while True:
-            more = self.step()
-            if not more or (max_steps is not None and self.steps >= max_steps):
+            last = max_steps is not None and self.steps + 1 >= max_steps
+            more = self.step(force_gather=last)
+            if not more or last:
                 return self.outputs
