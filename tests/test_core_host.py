@@ -244,3 +244,46 @@ def test_scheduler_watermark_keeps_reserve():
     out = sched.schedule()
     # 4 blocks fit under the 5-block reserve line, the next 2 would not.
     assert [g.group_id for g in out.scheduled_groups] == [0]
+
+
+def test_block_id_arrays_follow_appends_swaps_and_forks():
+    """The int32 id arrays a decode step copies equal the block lists after
+    every kind of change: appends across page boundaries, swap out and in
+    (new physical blocks), fork (shared blocks) and free."""
+    import numpy as np
+
+    from vllm_mps_b200.core.kv_cache_manager import KVCacheManager
+
+    m = KVCacheManager(64, 32)
+
+    def same(sid):
+        want = m.get_block_table(sid)
+        got = m.get_block_ids(sid)
+        assert got.dtype == np.int32 and got.tolist() == want
+        assert not got.flags.writeable
+
+    m.allocate(0)
+    m.allocate(1)
+    for t in range(300):  # 19 pages, past the array's first capacity of 16
+        m.append_slot(0)
+        if t % 3 == 0:
+            m.append_slot(1)
+        same(0)
+        same(1)
+    m.swap_out(0)
+    same(0)
+    m.swap_in(0)
+    same(0)
+    m.append_slot(0)
+    same(0)
+    m.fork(1, 2)
+    same(2)
+    for _ in range(40):
+        m.append_slot(2)
+    same(2)
+    same(1)
+    m.free(0)
+    m.allocate(0)
+    same(0)
+    m.append_slot(0)
+    same(0)

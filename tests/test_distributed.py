@@ -220,3 +220,28 @@ def _capacity_worker(rank, world, path, result_dir):
 def test_record_capacity_is_enforced_before_the_collective():
     d = _spawn(_capacity_worker, 1)
     assert open(os.path.join(d, "r0.txt")).read() == "capacity"
+
+
+def _max_steps_worker(rank, world, path, result_dir, every):
+    _init(rank, world, path)
+    prompts, params = _workload()
+    eng = ShardedEngine(FakeEngine(batch=3), gather_every=every)
+    eng.add_requests(prompts, params)
+    outs = eng.run(max_steps=6)
+    torch.save({"steps": eng.steps, "tokens": {g: o.token_ids for g, o in outs.items()}},
+               os.path.join(result_dir, f"r{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_max_steps_ends_on_a_gather_without_losing_buffered_tokens():
+    """run(max_steps) forces a gather on its last step, so tokens buffered
+    between gathers reach every rank: 6 steps with gathers every 4 steps give
+    the same tokens as 6 steps with a gather after each."""
+    got = {}
+    for every in (1, 4):
+        d = _spawn(_max_steps_worker, 2, every)
+        got[every] = [torch.load(os.path.join(d, f"r{r}.pt")) for r in range(2)]
+    for r in range(2):
+        assert got[4][r]["steps"] == got[1][r]["steps"] == 6
+        assert got[4][r]["tokens"] == got[1][0]["tokens"]
+    assert any(got[1][0]["tokens"].values())
