@@ -141,7 +141,7 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const GemmParams p)
           const int row = rb * kGemmRows + (half ? p.N : 0);
           const int kt = half ? s - p.kt : s;
           mbar_arrive_expect_tx(&full_bar[stage], kGemmStageBytes);
-          // Box {64 elements, 8 rows, kGemmKTile / 64 chunks}: chunks past K read
+          // Box {64 elements, kGemmRows rows, kGemmKTile / 64 chunks}: chunks past K read
           // as zeros.
           tma_load_3d(ring + stage * kGemmStageBytes, &wmap, &full_bar[stage], 0, row,
                       kt * (kGemmKTile / 64));
@@ -336,7 +336,7 @@ extern "C" int vmps_decode_gemm(void* out, int64_t out_row_stride, const void* x
   }
   const int wrows = silu_mul ? 2 * N : N;
   CUtensorMap wmap;
-  // W as {64 elements, rows, K / 64 chunks}: one box is 8 rows x 512 K.
+  // W as {64 elements, rows, K / 64 chunks}: one box is kGemmRows rows x kGemmKTile K.
   const uint64_t dims[3] = {64, (uint64_t)wrows, (uint64_t)((K + 63) / 64)};
   const uint64_t strides[2] = {(uint64_t)K * 2, 128};
   const uint32_t box[3] = {64, (uint32_t)kGemmRows, (uint32_t)(kGemmKTile / 64)};
