@@ -39,7 +39,7 @@ def test_block_errors_and_reset():
     b.add_tokens(5)
     b.reset()
     assert (b.ref_count, b.num_tokens) == (0, 0)
-    assert "block_id=0" in repr(b)
+    assert "block 0" in repr(b)
 
 
 # ── BlockAllocator ───────────────────────────────────────────────────────────
@@ -48,7 +48,7 @@ def test_allocator_fifo_order_and_reuse_after_fresh_ids():
     a = BlockAllocator(BlockAllocatorType.GPU, 4)
     got = [a.allocate().block_id for _ in range(3)]
     assert got == [0, 1, 2]
-    a.free(a._all_blocks[1])
+    a.free(a.block(1))
     # The freed id goes to the back: fresh id 3 comes first.
     assert a.allocate().block_id == 3
     assert a.allocate().block_id == 1
@@ -131,7 +131,7 @@ def test_kv_manager_fork_and_swap_accounting():
         m.append_slot(0)
     m.fork(0, 1)
     assert m.get_block_table(0) == m.get_block_table(1)
-    assert all(b.ref_count == 2 for b in m._block_tables[0]._blocks)
+    assert all(m.gpu_allocator.block(b).ref_count == 2 for b in m.get_block_table(0))
     with pytest.raises(ValueError):
         m.fork(0, 1)
     m.free(0)
@@ -287,3 +287,48 @@ def test_block_id_arrays_follow_appends_swaps_and_forks():
     same(0)
     m.append_slot(0)
     same(0)
+
+
+def test_bulk_slot_appends_equal_single_appends():
+    """append_slots(n) takes the same blocks, in the same FIFO order, with the
+    same fills as n calls of append_slot -- including when the pool runs out
+    part-way (the MemoryError comes at the same slot, with the same state)."""
+    import numpy as np
+
+    rng = np.random.default_rng(3)
+    a, b = KVCacheManager(40, 8), KVCacheManager(40, 8)
+    live = []
+    for step in range(200):
+        op = rng.integers(0, 4)
+        if op == 0 or not live:
+            sid = step
+            a.allocate(sid)
+            b.allocate(sid)
+            live.append(sid)
+        elif op == 1:
+            sid = live[rng.integers(len(live))]
+            n = int(rng.integers(1, 60))
+            ea = eb = None
+            try:
+                a.append_slots(sid, n)
+            except MemoryError as e:
+                ea = e
+            try:
+                for _ in range(n):
+                    b.append_slot(sid)
+            except MemoryError as e:
+                eb = e
+            assert (ea is None) == (eb is None)
+        elif op == 2:
+            sid = live.pop(rng.integers(len(live)))
+            a.free(sid)
+            b.free(sid)
+        else:
+            sid = live[rng.integers(len(live))]
+            assert a.free_slots_in_last_block(sid) == b.free_slots_in_last_block(sid)
+        for sid in live:
+            assert a.get_block_table(sid) == b.get_block_table(sid)
+            assert a.num_tokens(sid) == b.num_tokens(sid)
+        assert a.gpu_allocator.get_all_free_block_ids() == b.gpu_allocator.get_all_free_block_ids()
+        assert np.array_equal(a.gpu_allocator.counters.fill, b.gpu_allocator.counters.fill)
+        assert np.array_equal(a.gpu_allocator.counters.ref, b.gpu_allocator.counters.ref)

@@ -1,19 +1,30 @@
-"""FIFO block allocator (same contract as the reference's core/block_allocator.py).
+"""Block allocator over a fixed pool: int32 counter arrays and a FIFO ring of free ids.
 
-Blocks are handed out from the front of a FIFO free list and returned to its
-back, so a freed id is reused only after every never-used id has been handed
-out (block_allocator.py:85, :204).  Slot indices therefore match the
-reference bit for bit for the same operation stream.
+Contract (reference ``core/block_allocator.py:20-150``): ``allocate`` hands out
+the free block that has waited longest (a fresh pool hands out 0, 1, 2, ...;
+a freed id joins the back of the queue), with one reference; ``free`` drops a
+reference and queues the block again when none is left; ``fork`` adds a
+reference; ``MemoryError`` when nothing is free; counts and utilisation.
+That FIFO order is what makes slot indices identical to the reference's for
+the same operation stream.
+
+Layout: the free ids sit in an int32 ring buffer of ``total_blocks`` entries
+(``head`` = oldest, ``n_free`` live entries), reference counts and fill
+counts in the :class:`BlockCounters` arrays, one entry per block id.  The
+integer methods (``take``, ``take_many``, ``release``) are what the block
+tables use; ``allocate``/``free``/``fork`` keep the reference's
+block-object interface on top of them.
 """
 
 from __future__ import annotations
 
 import logging
-from collections import deque
 from enum import Enum
 
+import numpy as np
+
 from vllm_mps_b200.config import BLOCK_SIZE
-from vllm_mps_b200.core.block import PhysicalBlock
+from vllm_mps_b200.core.block import BlockCounters, PhysicalBlock
 
 logger = logging.getLogger(__name__)
 
@@ -26,55 +37,110 @@ class BlockAllocatorType(Enum):
 
 
 class BlockAllocator:
-    """Fixed pool of :class:`PhysicalBlock` descriptors with a FIFO free list."""
+    """``total_blocks`` block ids handed out in FIFO order."""
 
     def __init__(self, allocator_type: BlockAllocatorType, total_blocks: int) -> None:
+        n = int(total_blocks)
+        if n < 0:
+            raise ValueError(f"a pool cannot have {n} blocks")
         self.allocator_type = allocator_type
-        self.total_blocks = total_blocks
+        self.total_blocks = n
         self.block_size = BLOCK_SIZE
-        self._all_blocks: dict[int, PhysicalBlock] = {
-            i: PhysicalBlock(block_id=i) for i in range(total_blocks)}
-        self._free_list: deque[int] = deque(range(total_blocks))
-        logger.info("BlockAllocator [%s] initialised with %d blocks of size %d",
-                    allocator_type.value, total_blocks, self.block_size)
+        self.counters = BlockCounters(n, BLOCK_SIZE)
+        self._ring = np.arange(n, dtype=np.int32)
+        self._head = 0
+        self._n_free = n
+        self._handles: dict[int, PhysicalBlock] = {}
+        logger.debug("%s pool: %d blocks of %d slots", allocator_type.value, n, BLOCK_SIZE)
+
+    # ── integer interface ────────────────────────────────────────────────────
+
+    def _out_of_blocks(self) -> MemoryError:
+        return MemoryError(f"{self.allocator_type.value} pool exhausted: all "
+                           f"{self.total_blocks} blocks are in use")
+
+    def take(self) -> int:
+        """Pop the oldest free id and give it one reference."""
+        if self._n_free == 0:
+            raise self._out_of_blocks()
+        bid = int(self._ring[self._head])
+        self._head += 1
+        if self._head == self.total_blocks:
+            self._head = 0
+        self._n_free -= 1
+        self.counters.ref[bid] = 1
+        return bid
+
+    def take_many(self, k: int) -> np.ndarray:
+        """The next ``k`` free ids in FIFO order (as ``k`` calls of :meth:`take`)."""
+        if k > self._n_free:
+            raise self._out_of_blocks()
+        idx = (self._head + np.arange(k)) % max(self.total_blocks, 1)
+        ids = self._ring[idx].copy()
+        self._head = (self._head + k) % max(self.total_blocks, 1)
+        self._n_free -= k
+        self.counters.ref[ids] = 1
+        return ids
+
+    def release(self, bid: int) -> None:
+        """Drop one reference of ``bid``; when none is left, empty it and queue it last."""
+        ref = self.counters.ref
+        if ref[bid] <= 0:
+            raise ValueError(f"block {bid} of the {self.allocator_type.value} pool is already free")
+        ref[bid] -= 1
+        if ref[bid] == 0:
+            self.counters.fill[bid] = 0
+            self._ring[(self._head + self._n_free) % self.total_blocks] = bid
+            self._n_free += 1
+
+    def share(self, bid: int) -> None:
+        """One more reference on a block in use (copy-on-write sharing)."""
+        if not 0 <= bid < self.total_blocks:
+            raise ValueError(f"block {bid} is outside the {self.allocator_type.value} pool "
+                             f"(0..{self.total_blocks - 1})")
+        self.counters.ref[bid] += 1
+
+    def block(self, bid: int) -> PhysicalBlock:
+        """The handle of block ``bid`` (one per id, created on first use)."""
+        h = self._handles.get(bid)
+        if h is None:
+            h = PhysicalBlock(bid, counters=self.counters, index=bid)
+            self._handles[bid] = h
+        return h
+
+    # ── block-object interface ───────────────────────────────────────────────
 
     def allocate(self) -> PhysicalBlock:
-        """Pop the oldest free block (ref_count 1); ``MemoryError`` when empty."""
-        if not self._free_list:
-            raise MemoryError(f"BlockAllocator [{self.allocator_type.value}]: "
-                              f"out of memory. 0 free blocks remaining.")
-        block = self._all_blocks[self._free_list.popleft()]
-        block.increment_ref()
-        return block
+        return self.block(self.take())
 
     def free(self, block: PhysicalBlock) -> None:
-        """Drop one reference; at zero the block is reset and queued at the back."""
-        block.decrement_ref()
-        if block.is_free:
-            block.reset()
-            self._free_list.append(block.block_id)
+        if block._ctr is not self.counters:
+            raise ValueError(f"block {block.block_id} does not belong to the "
+                             f"{self.allocator_type.value} pool")
+        self.release(block.block_id)
 
     def fork(self, block: PhysicalBlock) -> PhysicalBlock:
-        """Share ``block`` copy-on-write (one more reference, no new block)."""
-        if block.block_id not in self._all_blocks:
-            raise ValueError(f"BlockAllocator [{self.allocator_type.value}]: "
-                             f"block {block.block_id} is not managed by this allocator.")
-        block.increment_ref()
-        return block
+        self.share(block.block_id)
+        return self.block(block.block_id)
+
+    # ── counts ───────────────────────────────────────────────────────────────
 
     def get_num_free_blocks(self) -> int:
-        return len(self._free_list)
+        return self._n_free
 
     def get_num_used_blocks(self) -> int:
-        return self.total_blocks - len(self._free_list)
+        return self.total_blocks - self._n_free
 
     def get_utilisation(self) -> float:
-        return self.get_num_used_blocks() / self.total_blocks
+        return self.get_num_used_blocks() / self.total_blocks if self.total_blocks else 0.0
 
     def get_all_free_block_ids(self) -> list[int]:
-        return list(self._free_list)
+        """Free ids, the next to be handed out first."""
+        if not self._n_free:
+            return []
+        idx = (self._head + np.arange(self._n_free)) % self.total_blocks
+        return self._ring[idx].tolist()
 
     def __repr__(self) -> str:
-        return (f"BlockAllocator(type={self.allocator_type.value}, total={self.total_blocks}, "
-                f"free={self.get_num_free_blocks()}, used={self.get_num_used_blocks()}, "
-                f"utilisation={self.get_utilisation():.1%})")
+        return (f"<{self.allocator_type.value} allocator: {self.get_num_used_blocks()} of "
+                f"{self.total_blocks} blocks used>")

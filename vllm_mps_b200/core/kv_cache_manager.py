@@ -1,21 +1,24 @@
-"""KV-cache manager: the single entry point for slot bookkeeping.
+"""KV-cache manager: every sequence's page table over a GPU and a CPU block pool.
 
-Same contract and the same slot assignment as the reference's
-core/kv_cache_manager.py:21-298 (tests replay a recorded op stream of the
-reference and require identical block tables after every operation).
+Contract (reference ``core/kv_cache_manager.py:21-298``): ``can_allocate``
+(read-only lookahead), ``allocate``/``append_slot``/``free`` of a sequence's
+table, ``fork`` (the child shares the parent's blocks by reference count),
+``swap_out``/``swap_in`` (each block moves to the other pool, in table order,
+keeping its fill), ``get_block_table`` and pool counts.  Unknown sequences
+raise ``KeyError``, duplicates ``ValueError``; a full pool ``MemoryError``.
+``tests/test_slot_traces.py`` replays the reference's own recorded op streams
+and requires identical tables and free counts after every operation.
 
-Swap-out/in in the reference moves block *metadata* only; the KV data of a
-preempted sequence is lost (kv_cache_manager.py:188, :225).  That stays the
-default.  Attaching a ``swap_space`` (any object with ``copy_out(gpu_ids,
-cpu_ids)`` and ``copy_in(cpu_ids, gpu_ids)``, e.g.
-:class:`vllm_mps_b200.memory.cuda_memory_pool.SwapSpace`) makes swapping
-carry the data too, without changing which block ids are chosen.
+The reference moves only block metadata on a swap, so a preempted
+sequence's K/V is lost.  That stays the default; a ``swap_space`` (any
+object with ``copy_out(gpu_ids, cpu_ids)`` and ``copy_in(cpu_ids, gpu_ids)``,
+e.g. :class:`vllm_mps_b200.memory.cuda_memory_pool.SwapSpace`) makes the
+swap carry the data too, without changing which ids are chosen.
 """
 
 from __future__ import annotations
 
 import logging
-import math
 
 from vllm_mps_b200.config import BLOCK_SIZE
 from vllm_mps_b200.core.block import PhysicalBlock
@@ -26,134 +29,123 @@ logger = logging.getLogger(__name__)
 
 
 class KVCacheManager:
-    """Coordinates the GPU/CPU block allocators and the per-sequence tables."""
+    """Page tables of all live sequences over a GPU pool and a CPU swap pool."""
 
     def __init__(self, num_gpu_blocks: int, num_cpu_blocks: int, swap_space=None) -> None:
         self.block_size = BLOCK_SIZE
-        self._gpu_allocator = BlockAllocator(BlockAllocatorType.GPU, num_gpu_blocks)
-        self._cpu_allocator = BlockAllocator(BlockAllocatorType.CPU, num_cpu_blocks)
-        self._block_tables: dict[int, BlockTable] = {}
+        self.gpu_allocator = BlockAllocator(BlockAllocatorType.GPU, num_gpu_blocks)
+        self.cpu_allocator = BlockAllocator(BlockAllocatorType.CPU, num_cpu_blocks)
+        self._tables: dict[int, BlockTable] = {}
         self.swap_space = swap_space
-        logger.info("KVCacheManager: GPU=%d blocks, CPU=%d blocks, block_size=%d",
-                    num_gpu_blocks, num_cpu_blocks, self.block_size)
+
+    def _table(self, seq_id: int) -> BlockTable:
+        t = self._tables.get(seq_id)
+        if t is None:
+            raise KeyError(f"no page table for sequence {seq_id}")
+        return t
 
     # ── lookahead ────────────────────────────────────────────────────────────
 
+    def free_slots_in_last_block(self, seq_id: int) -> int:
+        """Slots a sequence can still fill without a new block (0 if it has no table)."""
+        t = self._tables.get(seq_id)
+        return t.last_block_room() if t is not None else 0
+
+    def blocks_needed(self, seq_id: int, num_tokens: int) -> int:
+        """New GPU blocks that ``num_tokens`` more tokens of ``seq_id`` would take."""
+        extra = num_tokens - self.free_slots_in_last_block(seq_id)
+        return -(-extra // self.block_size) if extra > 0 else 0
+
     def can_allocate(self, seq_id: int, num_tokens: int) -> bool:
-        """Read-only check that ``num_tokens`` more slots fit (kv_cache_manager.py:53-77)."""
-        if seq_id in self._block_tables:
-            table = self._block_tables[seq_id]
-            empty = table.get_last_block().num_empty_slots if not table.is_empty() else 0
-            need_tokens = max(0, num_tokens - empty)
-        else:
-            need_tokens = num_tokens
-        return math.ceil(need_tokens / self.block_size) <= self._gpu_allocator.get_num_free_blocks()
+        return self.blocks_needed(seq_id, num_tokens) <= self.gpu_allocator.get_num_free_blocks()
 
     # ── lifecycle ────────────────────────────────────────────────────────────
 
+    def has_sequence(self, seq_id: int) -> bool:
+        return seq_id in self._tables
+
     def allocate(self, seq_id: int) -> None:
-        if seq_id in self._block_tables:
-            raise ValueError(f"KVCacheManager: seq_id {seq_id} already exists.")
-        self._block_tables[seq_id] = BlockTable(seq_id, self._gpu_allocator)
-        logger.info("KVCacheManager: allocated table for seq=%d", seq_id)
+        if seq_id in self._tables:
+            raise ValueError(f"sequence {seq_id} already has a page table")
+        self._tables[seq_id] = BlockTable(seq_id, self.gpu_allocator)
 
     def append_slot(self, seq_id: int) -> PhysicalBlock:
-        if seq_id not in self._block_tables:
-            raise KeyError(f"KVCacheManager: seq_id {seq_id} not found.")
-        return self._block_tables[seq_id].append_slot()
+        return self._table(seq_id).append_slot()
+
+    def append_slots(self, seq_id: int, n: int) -> None:
+        """``n`` calls of :meth:`append_slot` (a prompt's slots) in one go."""
+        self._table(seq_id).append_slots(n)
 
     def free(self, seq_id: int) -> None:
-        if seq_id not in self._block_tables:
-            raise KeyError(f"KVCacheManager: seq_id {seq_id} not found.")
-        self._block_tables[seq_id].free_all()
-        del self._block_tables[seq_id]
-        logger.info("KVCacheManager: freed table for seq=%d", seq_id)
+        self._table(seq_id).free_all()
+        del self._tables[seq_id]
 
     def fork(self, parent_seq_id: int, child_seq_id: int) -> None:
-        """Child shares the parent's blocks copy-on-write (:134-172)."""
-        if parent_seq_id not in self._block_tables:
-            raise KeyError(f"KVCacheManager: parent seq_id {parent_seq_id} not found.")
-        if child_seq_id in self._block_tables:
-            raise ValueError(f"KVCacheManager: child seq_id {child_seq_id} already exists.")
-        parent = self._block_tables[parent_seq_id]
-        child = BlockTable(child_seq_id, self._gpu_allocator)
-        for block in parent._blocks:
-            self._gpu_allocator.fork(block)
-        child.replace_blocks(list(parent._blocks))
-        child._num_tokens = parent._num_tokens
-        self._block_tables[child_seq_id] = child
-        logger.info("KVCacheManager: forked seq=%d -> seq=%d, %d blocks shared",
-                    parent_seq_id, child_seq_id, len(parent._blocks))
+        parent = self._table(parent_seq_id)
+        if child_seq_id in self._tables:
+            raise ValueError(f"sequence {child_seq_id} already has a page table")
+        ids = parent.block_ids().copy()
+        for bid in ids.tolist():
+            parent.allocator.share(bid)
+        child = BlockTable(child_seq_id, parent.allocator)
+        child.adopt(ids, parent.num_tokens(), parent.allocator)
+        self._tables[child_seq_id] = child
 
     # ── swap (GPU <-> CPU) ───────────────────────────────────────────────────
 
+    def _move(self, seq_id: int, src: BlockAllocator, dst: BlockAllocator) -> list[tuple[int, int]]:
+        """Give every block of ``seq_id`` a ``dst`` block with the same fill; free the ``src`` one."""
+        t = self._table(seq_id)
+        moved = []
+        for bid in t.block_ids().tolist():
+            nid = dst.take()
+            dst.counters.fill[nid] += src.counters.fill[bid]
+            src.release(bid)
+            moved.append((bid, nid))
+        t.adopt([n for _, n in moved], t.num_tokens(), dst)
+        return moved
+
     def swap_out(self, seq_id: int) -> None:
-        """Move a sequence's blocks to the CPU pool (:176-211), data too if a swap space is set."""
-        if seq_id not in self._block_tables:
-            raise KeyError(f"KVCacheManager: seq_id {seq_id} not found.")
-        table = self._block_tables[seq_id]
-        new_blocks, pairs = [], []
-        for gpu_block in table._blocks:
-            cpu_block = self._cpu_allocator.allocate()
-            cpu_block.add_tokens(gpu_block.num_tokens)
-            pairs.append((gpu_block.block_id, cpu_block.block_id))
-            self._gpu_allocator.free(gpu_block)
-            new_blocks.append(cpu_block)
-        if self.swap_space is not None and pairs:
-            self.swap_space.copy_out([g for g, _ in pairs], [c for _, c in pairs])
-        table.replace_blocks(new_blocks)
-        table._allocator = self._cpu_allocator
-        logger.info("KVCacheManager: swapped out seq=%d, %d blocks to CPU", seq_id, len(pairs))
+        moved = self._move(seq_id, self.gpu_allocator, self.cpu_allocator)
+        if self.swap_space is not None and moved:
+            self.swap_space.copy_out([g for g, _ in moved], [c for _, c in moved])
+        logger.debug("sequence %d: %d blocks moved to the CPU pool", seq_id, len(moved))
 
     def swap_in(self, seq_id: int) -> None:
-        """Move a sequence's blocks back to the GPU pool (:213-248)."""
-        if seq_id not in self._block_tables:
-            raise KeyError(f"KVCacheManager: seq_id {seq_id} not found.")
-        table = self._block_tables[seq_id]
-        new_blocks, pairs = [], []
-        for cpu_block in table._blocks:
-            gpu_block = self._gpu_allocator.allocate()
-            gpu_block.add_tokens(cpu_block.num_tokens)
-            pairs.append((cpu_block.block_id, gpu_block.block_id))
-            self._cpu_allocator.free(cpu_block)
-            new_blocks.append(gpu_block)
-        if self.swap_space is not None and pairs:
-            self.swap_space.copy_in([c for c, _ in pairs], [g for _, g in pairs])
-        table.replace_blocks(new_blocks)
-        table._allocator = self._gpu_allocator
-        logger.info("KVCacheManager: swapped in seq=%d, %d blocks to GPU", seq_id, len(pairs))
+        moved = self._move(seq_id, self.cpu_allocator, self.gpu_allocator)
+        if self.swap_space is not None and moved:
+            self.swap_space.copy_in([c for c, _ in moved], [g for _, g in moved])
+        logger.debug("sequence %d: %d blocks moved back to the GPU pool", seq_id, len(moved))
 
     # ── introspection ────────────────────────────────────────────────────────
 
     def get_block_ids(self, seq_id: int):
-        """``get_block_table`` as a read-only int32 numpy array (no per-call list)."""
-        if seq_id not in self._block_tables:
-            raise KeyError(f"KVCacheManager: seq_id {seq_id} not found.")
-        return self._block_tables[seq_id].block_ids()
+        """The block table of ``seq_id`` as a read-only int32 array."""
+        return self._table(seq_id).block_ids()
 
     def get_block_table(self, seq_id: int) -> list[int]:
-        """Ordered physical block ids of ``seq_id`` (:252-265)."""
-        if seq_id not in self._block_tables:
-            raise KeyError(f"KVCacheManager: seq_id {seq_id} not found.")
-        return self._block_tables[seq_id].get_all_physical_block_ids()
+        return self._table(seq_id).get_all_physical_block_ids()
+
+    def num_tokens(self, seq_id: int) -> int:
+        """Token slots held by ``seq_id``."""
+        return self._table(seq_id).num_tokens()
 
     def get_num_free_gpu_blocks(self) -> int:
-        return self._gpu_allocator.get_num_free_blocks()
+        return self.gpu_allocator.get_num_free_blocks()
 
     def get_num_free_cpu_blocks(self) -> int:
-        return self._cpu_allocator.get_num_free_blocks()
+        return self.cpu_allocator.get_num_free_blocks()
 
     def get_gpu_utilisation(self) -> float:
-        return self._gpu_allocator.get_utilisation()
+        return self.gpu_allocator.get_utilisation()
 
     def get_cpu_utilisation(self) -> float:
-        return self._cpu_allocator.get_utilisation()
+        return self.cpu_allocator.get_utilisation()
 
     def get_all_seq_ids(self) -> list[int]:
-        return list(self._block_tables.keys())
+        return list(self._tables)
 
     def __repr__(self) -> str:
-        return (f"KVCacheManager(seqs={len(self._block_tables)}, "
-                f"GPU free={self.get_num_free_gpu_blocks()}/{self._gpu_allocator.total_blocks}, "
-                f"CPU free={self.get_num_free_cpu_blocks()}/{self._cpu_allocator.total_blocks}, "
-                f"GPU util={self.get_gpu_utilisation():.1%}, CPU util={self.get_cpu_utilisation():.1%})")
+        g, c = self.gpu_allocator, self.cpu_allocator
+        return (f"<KV cache: {len(self._tables)} sequences, GPU {g.get_num_used_blocks()}/"
+                f"{g.total_blocks} blocks used, CPU {c.get_num_used_blocks()}/{c.total_blocks}>")

@@ -1,4 +1,12 @@
-"""Request state (same contract as the reference's core/sequence.py:14-216)."""
+"""Requests: sampling settings, one sequence's tokens and state, groups of sequences.
+
+Contract (reference ``core/sequence.py:14-216``): the four statuses, the
+``SamplingParams`` fields with their defaults and validity ranges (a bad
+value raises ``ValueError``), ``Sequence.add_token`` finishing a sequence
+once ``max_tokens`` tokens have been generated, the length getters,
+``get_last_token_id`` (``IndexError`` when empty), and ``SequenceGroup``'s
+status filters.
+"""
 
 from __future__ import annotations
 
@@ -16,7 +24,7 @@ class SequenceStatus(Enum):
 
 @dataclass
 class SamplingParams:
-    """Sampling configuration (temperature 0 = greedy), validated like :41-61."""
+    """temperature 0 = greedy; top_k 0 = off; top_p 1 = off."""
 
     temperature: float = 1.0
     top_k: int = 0
@@ -25,60 +33,66 @@ class SamplingParams:
     stop_sequences: list[str] = field(default_factory=list)
 
     def __post_init__(self) -> None:
-        if self.temperature < 0.0:
-            raise ValueError(f"SamplingParams: temperature must be >= 0.0, got {self.temperature}.")
+        bad = []
+        if not self.temperature >= 0.0:
+            bad.append(f"temperature={self.temperature} (needs >= 0)")
         if self.top_k < 0:
-            raise ValueError(f"SamplingParams: top_k must be >= 0, got {self.top_k}.")
-        if not (0.0 < self.top_p <= 1.0):
-            raise ValueError(f"SamplingParams: top_p must be in (0.0, 1.0], got {self.top_p}.")
+            bad.append(f"top_k={self.top_k} (needs >= 0)")
+        if not 0.0 < self.top_p <= 1.0:
+            bad.append(f"top_p={self.top_p} (needs 0 < top_p <= 1)")
         if self.max_tokens < 1:
-            raise ValueError(f"SamplingParams: max_tokens must be >= 1, got {self.max_tokens}.")
+            bad.append(f"max_tokens={self.max_tokens} (needs >= 1)")
+        if bad:
+            raise ValueError("invalid sampling parameters: " + ", ".join(bad))
 
 
 class Sequence:
-    """One request's tokens (prompt + generated) and its lifecycle state."""
+    """Prompt plus generated token ids of one request, and where it is in its life."""
 
     def __init__(self, seq_id: int, prompt: str, token_ids: list[int],
                  sampling_params: SamplingParams) -> None:
         self.seq_id = seq_id
         self.prompt = prompt
         self.token_ids = list(token_ids)
+        self.prompt_len = len(self.token_ids)
         self.sampling_params = sampling_params
         self.status = SequenceStatus.WAITING
         self.arrival_time = time.time()
-        self._prompt_len = len(token_ids)
-        self._output_token_ids: list[int] = []
+
+    @property
+    def output_token_ids(self) -> list[int]:
+        """The generated tokens (everything after the prompt)."""
+        return self.token_ids[self.prompt_len:]
 
     def add_token(self, token_id: int) -> None:
-        """Append a generated token; finish at ``max_tokens`` (:103-113)."""
         self.token_ids.append(token_id)
-        self._output_token_ids.append(token_id)
-        if len(self._output_token_ids) >= self.sampling_params.max_tokens:
+        if len(self.token_ids) - self.prompt_len >= self.sampling_params.max_tokens:
             self.status = SequenceStatus.FINISHED
 
     def get_prompt_len(self) -> int:
-        return self._prompt_len
+        return self.prompt_len
 
     def get_output_len(self) -> int:
-        return len(self._output_token_ids)
+        return len(self.token_ids) - self.prompt_len
 
     def get_total_len(self) -> int:
         return len(self.token_ids)
 
     def is_finished(self) -> bool:
-        return self.status == SequenceStatus.FINISHED
+        return self.status is SequenceStatus.FINISHED
 
     def get_last_token_id(self) -> int:
         if not self.token_ids:
-            raise IndexError(f"Sequence [seq={self.seq_id}]: token_ids is empty.")
+            raise IndexError(f"sequence {self.seq_id} has no tokens")
         return self.token_ids[-1]
 
     def __repr__(self) -> str:
-        return f"Sequence(seq_id={self.seq_id}, status={self.status.value}, total_len={self.get_total_len()})"
+        return (f"<seq {self.seq_id} {self.status.value}: {self.prompt_len} prompt + "
+                f"{self.get_output_len()} generated tokens>")
 
 
 class SequenceGroup:
-    """Related sequences sharing sampling parameters (:156-216)."""
+    """Sequences of one request that share sampling settings."""
 
     def __init__(self, group_id: int, sequences: list[Sequence],
                  sampling_params: SamplingParams) -> None:
@@ -90,10 +104,12 @@ class SequenceGroup:
     def get_seqs(self, status: SequenceStatus | None = None) -> list[Sequence]:
         if status is None:
             return list(self.sequences)
-        return [s for s in self.sequences if s.status == status]
+        return [s for s in self.sequences if s.status is status]
 
     def get_num_seqs(self, status: SequenceStatus | None = None) -> int:
-        return len(self.get_seqs(status))
+        if status is None:
+            return len(self.sequences)
+        return sum(1 for s in self.sequences if s.status is status)
 
     def is_finished(self) -> bool:
         return all(s.is_finished() for s in self.sequences)
@@ -102,5 +118,5 @@ class SequenceGroup:
         return max(s.get_total_len() for s in self.sequences)
 
     def __repr__(self) -> str:
-        return (f"SequenceGroup(group_id={self.group_id}, num_seqs={len(self.sequences)}, "
-                f"finished={self.is_finished()})")
+        state = "finished" if self.is_finished() else "live"
+        return f"<group {self.group_id}: {len(self.sequences)} sequences, {state}>"

@@ -179,8 +179,9 @@ class LLMEngine:
         # Give every scheduled sequence a slot for each of its tokens.
         kv = self.kv_cache_manager
         for s in seqs:
-            while kv._block_tables[s.seq_id].num_tokens() < s.get_total_len():
-                kv.append_slot(s.seq_id)
+            short = s.get_total_len() - kv.num_tokens(s.seq_id)
+            if short > 0:
+                kv.append_slots(s.seq_id, short)
         if self.mode == "physical":
             self._prefill([s for s in seqs if s.seq_id not in self._prefilled])
         seq_ids = [s.seq_id for s in seqs]
@@ -260,9 +261,9 @@ class LLMEngine:
                 for pl in self.adapter.paged_layers:
                     pl.evict_sequence(seq_id)
             out = self._outputs[request_id]
-            out.token_ids.append(token_id)  # mirrors seq._output_token_ids
+            out.token_ids.append(token_id)  # mirrors seq.output_token_ids
             if self.tokenizer is not None:
-                out.generated_text = self.tokenizer.decode(seq._output_token_ids,
+                out.generated_text = self.tokenizer.decode(seq.output_token_ids,
                                                            skip_special_tokens=True)
             out.finished = seq.is_finished()
             out.num_steps += 1

@@ -57,16 +57,10 @@ class Scheduler:
         kv = self.kv_cache_manager
         if self.preempt_watermark is None:
             return kv.can_allocate(seq_id, num_tokens)
-        # Same block arithmetic as KVCacheManager.can_allocate, minus the reserve.
-        if seq_id in kv._block_tables:
-            table = kv._block_tables[seq_id]
-            empty = table.get_last_block().num_empty_slots if not table.is_empty() else 0
-            need_tokens = max(0, num_tokens - empty)
-        else:
-            need_tokens = num_tokens
-        total = kv._gpu_allocator.total_blocks
+        # KVCacheManager.can_allocate's block arithmetic, minus the reserve.
+        total = kv.gpu_allocator.total_blocks
         reserve = int(math.floor(total * (1.0 - self.preempt_watermark)))
-        return math.ceil(need_tokens / kv.block_size) <= kv.get_num_free_gpu_blocks() - reserve
+        return kv.blocks_needed(seq_id, num_tokens) <= kv.get_num_free_gpu_blocks() - reserve
 
     def _free_beyond_reserve(self) -> int:
         """Free GPU blocks minus the watermark's reserve (the count _fits compares with)."""
@@ -74,7 +68,7 @@ class Scheduler:
         free = kv.get_num_free_gpu_blocks()
         if self.preempt_watermark is None:
             return free
-        total = kv._gpu_allocator.total_blocks
+        total = kv.gpu_allocator.total_blocks
         return free - int(math.floor(total * (1.0 - self.preempt_watermark)))
 
     def schedule(self) -> SchedulerOutput:
@@ -117,8 +111,7 @@ class Scheduler:
             self._waiting.popleft()
             for s in seqs:
                 self.kv_cache_manager.allocate(s.seq_id)
-                for _ in range(s.get_prompt_len()):
-                    self.kv_cache_manager.append_slot(s.seq_id)
+                self.kv_cache_manager.append_slots(s.seq_id, s.get_prompt_len())
                 s.status = SequenceStatus.RUNNING
             self._running.append(group)
             scheduled.append(group)
