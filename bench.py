@@ -78,17 +78,36 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
+KERNEL_SOURCES = ("vllm_mps_b200/csrc/paged_decode.cu", "vllm_mps_b200/csrc/vmps_common.cuh")
+
+
+def kernel_source_hash():
+    """sha256 over the decode kernel's source files (what an ncu capture measured)."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for rel in KERNEL_SOURCES:
+        with open(os.path.join(ROOT, rel), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
 def profile_traffic(cfg_name):
-    """DRAM bytes per launch of the attention kernel from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", f"paged_decode_{cfg_name}.md")
+    """ncu DRAM bytes per launch of the decode kernel on ``cfg_name``, or None.
+
+    profiles/decode_traffic.json holds, per config, the read + write bytes of
+    one launch from an ncu capture together with the sha256 of the kernel
+    sources it was captured from; after any change to those sources the
+    stored figure no longer describes the kernel and None is returned.
+    """
     try:
-        for line in open(path):
-            if line.startswith("traffic_bytes_per_launch:"):
-                val = line.split(":")[1].strip()
-                return None if val == "null" else int(val)
-    except OSError:
-        pass
-    return None
+        with open(os.path.join(ROOT, "profiles", "decode_traffic.json")) as f:
+            rec = json.load(f).get(cfg_name)
+    except (OSError, ValueError):
+        return None
+    if not rec or rec.get("kernel_source_sha256") != kernel_source_hash():
+        return None
+    return int(rec["traffic_bytes_per_launch"])
 
 
 def make_host_workload(cfg, seed):
@@ -107,6 +126,13 @@ def make_host_workload(cfg, seed):
             off += p
         tables.append(bt)
     return ctx, pages, tables
+
+
+def decode_config(cfg, ctx, world):
+    """The ``config`` object of a decode-step line (identical on both arms)."""
+    B, lo, hi, desc = cfg[0], cfg[5], cfg[6], cfg[9]
+    return {"workload": desc, "global_batch": B * world, "seq_len": "U[%d,%d]" % (lo, hi),
+            "sum_ctx_per_rank": int(ctx.sum()), "parallelism": f"sequence-sharded x{world}"}
 
 
 def alg_bytes(cfg, ctx, pages, fused=False):
@@ -269,7 +295,7 @@ def run_reference(args, cfg, rank, world):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16" if dt == "bfloat16" else "f16",
         "data": "synthetic (seeded)", "impl": "reference",
-        "config": {"workload": desc, "global_batch": B, "parallelism": "host cores"},
+        "config": decode_config(cfg, ctx, world),
         "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": c_oracle.max_threads(),
                          "kind": "port",
                          "sample": f"{len(sel)} of {B} sequences per step (sum ctx "
@@ -281,7 +307,9 @@ def run_reference(args, cfg, rank, world):
     return 0
 
 
-def run_ours(args, cfg, rank, world, local_rank):
+def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
+    """One decode-step config (c1/c2layer/c3): the record on rank 0, None elsewhere."""
+    cfg = CONFIGS[cfg_name]
     import torch
 
     from vllm_mps_b200 import kernels as K
@@ -338,16 +366,22 @@ def run_ours(args, cfg, rank, world, local_rank):
                 fn()
         return gr
 
-    g_steps = capture([lambda r=r: step(r) for r in range(R)])
-    g_step1 = [capture([lambda r=r: step(r)]) for r in range(R)]
-    g_attns = capture([lambda r=r: attn(r) for r in range(R)])
-    torch.cuda.synchronize(dev)
+    # The timed K steps are ONE graph of K PDL-chained launches (replicas
+    # rotating), so the timed region is one replay with no graph boundary
+    # between steps -- the steady state a serving loop sees.  The warm-up
+    # steps are a graph of their own.
+    graphs = {}
 
     def run_steps(n):
-        for _ in range(n // R):
-            g_steps.replay()
-        for r in range(n % R):
-            g_step1[r].replay()
+        if n not in graphs:
+            graphs[n] = capture([lambda i=i: step(i % R) for i in range(n)])
+            torch.cuda.synchronize(dev)
+        graphs[n].replay()
+
+    run_steps(args.warmup)
+    run_steps(args.steps)
+    g_attns = capture([lambda r=r: attn(r) for r in range(R)])
+    torch.cuda.synchronize(dev)
     if K.error_word(dev):
         raise RuntimeError("device error word set during warm-up")
 
@@ -516,12 +550,12 @@ def run_ours(args, cfg, rank, world, local_rank):
             "ms_per_step": t_step / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if dt == "bfloat16" else "f16",
             "data": "synthetic (seeded N(0,1) q/k/v/pool; seeded ragged contexts)",
-            "config": {
-                "workload": desc, "global_batch": B * world, "seq_len": "U[%d,%d]" % (lo, hi),
-                "sum_ctx_per_rank": int(ctx.sum()), "parallelism": f"sequence-sharded x{world}",
+            "config": decode_config(cfg, ctx, world),
+            "method": {
                 "l2": f"inputs larger than L2: {R} pool/table replicas rotated "
                       f"({R} x {ab / 1e6:.0f} MB touched per cycle)",
-                "timing": f"CUDA graphs of {R} steps (PDL-chained), CUDA events, max over ranks",
+                "timing": f"one CUDA graph of the {args.steps} timed steps (PDL-chained), CUDA "
+                          "events, max over ranks",
             },
             "e2e": {"value": world * B * e2e_steps / t_e2e, "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h,
@@ -530,7 +564,7 @@ def run_ours(args, cfg, rank, world, local_rank):
                            "packed pinned inputs and one D2H of the output, pipelined on two "
                            f"copy streams, CUDA graphs of {R} steps with their copy nodes"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": profile_traffic(args.config),
+                         "frac": achieved / peak, "traffic": profile_traffic(cfg_name),
                          "peak_kind": peak_kind,
                          "kernel": "paged_decode_kernel (fused decode step)",
                          "kernel_us": t_launch * 1e6, "alg_bytes_per_launch": ab,
@@ -541,10 +575,10 @@ def run_ours(args, cfg, rank, world, local_rank):
             "clocks": clocks.summary(),
             "gpu_launches": args.steps,
         }
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and cpu_base:
             line["cpu_baseline"] = cpu_baseline(cfg, ctx, tables)
-        print(json.dumps(line), flush=True)
-    return 0
+        return line
+    return None
 
 
 # ── prefill (kernel 3) ───────────────────────────────────────────────────────
@@ -603,14 +637,9 @@ def prefill_cpu_baseline(B, L, n_q, n_kv, D, dt, theta, budget_s=10.0):
                       f"(token-by-token, as the reference prefills), C oracle, OpenMP"}
 
 
-def run_prefill(args, rank, world, local_rank):
-    import torch
-
-    from vllm_mps_b200 import kernels as K
-    from vllm_mps_b200.layers.rotary_embedding import rope_inv_freq
-
+def run_prefill_reference(args, rank, world):
     B, L, n_q, n_kv, D, dtn, theta, desc = PREFILL[args.config]
-    if args.impl == "reference":
+    if True:
         if rank != 0:
             return 0
         base = prefill_cpu_baseline(B, L, n_q, n_kv, D, dtn, theta,
@@ -626,6 +655,16 @@ def run_prefill(args, rank, world, local_rank):
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}), flush=True)
         return 0
+
+
+def prefill_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
+    """Kernel 3 on a PREFILL config: the record on rank 0, None elsewhere."""
+    import torch
+
+    from vllm_mps_b200 import kernels as K
+    from vllm_mps_b200.layers.rotary_embedding import rope_inv_freq
+
+    B, L, n_q, n_kv, D, dtn, theta, desc = PREFILL[cfg_name]
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     dt = getattr(torch, dtn)
@@ -744,10 +783,10 @@ def run_prefill(args, rank, world, local_rank):
             "clocks": clocks.summary(),
             "gpu_launches": args.steps,
         }
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and cpu_base:
             line["cpu_baseline"] = prefill_cpu_baseline(B, L, n_q, n_kv, D, dtn, theta)
-        print(json.dumps(line), flush=True)
-    return 0
+        return line
+    return None
 
 
 # ── engine decode (configs 0 and 2) ─────────────────────────────────────────
@@ -885,8 +924,15 @@ C4 = ("Config 4: TinyLlama shape (config 0 model), 1024 requests, prompts "
       "is 90% full, sequence-sharded (one engine per GPU, NCCL token gather every 16 steps)")
 
 
-def run_c4(args, rank, world, local_rank):
-    """All 1024 requests to completion; generated tokens per second over the whole run."""
+def c4_leg(args, rank, world, local_rank, n_req=1024):
+    """All config-4 requests to completion through the sequence-sharded engine.
+
+    Every rank runs ``ShardedEngine`` over its own ``LLMEngine`` (at N = 1 the
+    same loop, without the collective); the ranks exchange their sampled
+    tokens with one NCCL ``all_gather_into_tensor`` every 16 steps.  Returns
+    the record on rank 0 (None elsewhere): generated tokens/s of the whole
+    job, steps, gathers, per-rank time in local steps and in the gathers.
+    """
     import torch
     from transformers import LlamaConfig, LlamaForCausalLM
 
@@ -905,7 +951,6 @@ def run_c4(args, rank, world, local_rank):
     with torch.device(dev):
         model = LlamaForCausalLM(cfg).to(torch.float16).eval()
     rng = np.random.default_rng(4)
-    n_req = 1024
     p_lens = np.clip(np.round(rng.lognormal(6, 1, n_req)), 16, 4096).astype(int)
     o_lens = rng.integers(16, 513, n_req)
     prompts = [rng.integers(0, vocab, size=int(n)).tolist() for n in p_lens]
@@ -924,7 +969,6 @@ def run_c4(args, rank, world, local_rank):
     while not eng.is_finished():
         eng.step()
     torch.cuda.synchronize(dev)
-    start_tokens = eng.total_tokens_generated
     if dist is not None:
         dist.barrier(device_ids=[local_rank])
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -936,46 +980,66 @@ def run_c4(args, rank, world, local_rank):
             sharded.add_requests(prompts, params)
             outs = sharded.run()
             done = sum(len(o.token_ids) for o in outs.values())
-            steps = sharded.steps
+            steps, gathers = sharded.steps, sharded.gathers
+            step_s, gather_s = sharded.step_seconds, sharded.gather_seconds
         else:
+            start_tokens = eng.total_tokens_generated
             for p, sp in zip(prompts, params):
                 eng.add_request(p, sp)
             steps = 0
+            t_s = time.perf_counter()
             while not eng.is_finished():
                 eng.step()
                 steps += 1
+            step_s, gather_s, gathers = time.perf_counter() - t_s, 0.0, 0
             done = eng.total_tokens_generated - start_tokens
         e1.record()
         torch.cuda.synchronize(dev)
     t = e0.elapsed_time(e1) * 1e-3
+    per_rank = np.array([[t, step_s, gather_s, steps]], dtype=np.float64)
     if dist is not None:
-        tt = torch.tensor([t], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t = float(tt[0])
+        mine = torch.tensor(per_rank[0], dtype=torch.float64, device=dev)
+        allr = torch.empty(world * 4, dtype=torch.float64, device=dev)
+        dist.all_gather_into_tensor(allr, mine)
+        per_rank = allr.view(world, 4).cpu().numpy()
+        t = float(per_rank[:, 0].max())
     from vllm_mps_b200 import kernels as K
 
     if K.error_word(dev):
         raise RuntimeError("device error word set during the config-4 run")
     if done != int(o_lens.sum()):
         raise RuntimeError(f"generated {done} tokens, expected {int(o_lens.sum())}")
-    if rank == 0:
-        line = {
-            "metric": "generated tokens/s (mixed prefill + decode)", "value": done / t,
-            "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": 1,
-            "ms_per_step": t / max(steps, 1) * 1e3, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f16",
-            "data": "synthetic (random-init weights, seeded lognormal prompts)",
-            "config": {"workload": C4, "global_batch": n_req, "parallelism":
-                       f"sequence-sharded x{world}", "prompt_tokens": int(p_lens.sum()),
-                       "generated_tokens": int(o_lens.sum()), "wall_s": time.perf_counter() - t_wall,
-                       "preempted_final": eng.scheduler.get_num_preempted(),
-                       "timing": "CUDA events around the whole run, max over ranks"},
-            "e2e": {"value": done / t, "unit": "tokens/s", "h2d_bytes_per_step": None,
-                    "d2h_bytes_per_step": None,
-                    "api": "LLMEngine / ShardedEngine: host token ids in and out"},
-            "roofline": None, "clocks": clocks.summary(), "gpu_launches": None,
-            "cpu_baseline": None,
-        }
+    if rank != 0:
+        return None
+    return {
+        "metric": "generated tokens/s (mixed prefill + decode)", "value": done / t,
+        "unit": "tokens/s", "n_gpus": world, "steps": steps, "gathers": gathers,
+        "ms_per_step": t / max(steps, 1) * 1e3, "higher_is_better": True,
+        "scaling": "strong", "dtype": "f16",
+        "data": "synthetic (random-init weights, seeded lognormal prompts)",
+        "config": {"workload": C4 if n_req == 1024 else f"{C4} [first {n_req} requests]",
+                   "global_batch": n_req, "parallelism": f"sequence-sharded x{world}",
+                   "prompt_tokens": int(p_lens.sum()), "generated_tokens": int(o_lens.sum()),
+                   "timing": "CUDA events around the whole run, max over ranks"},
+        "per_rank": {"run_s": per_rank[:, 0].round(4).tolist(),
+                     "local_step_s": per_rank[:, 1].round(4).tolist(),
+                     "gather_s": per_rank[:, 2].round(4).tolist(),
+                     "gather_share": (per_rank[:, 2] / np.maximum(per_rank[:, 0], 1e-9))
+                     .round(4).tolist()},
+        "wall_s": time.perf_counter() - t_wall,
+        "preempted_final": eng.scheduler.get_num_preempted(),
+        "e2e": {"value": done / t, "unit": "tokens/s", "h2d_bytes_per_step": None,
+                "d2h_bytes_per_step": None,
+                "api": "LLMEngine / ShardedEngine: host token ids in and out"},
+        "clocks": clocks.summary(),
+    }
+
+
+def run_c4(args, rank, world, local_rank):
+    line = c4_leg(args, rank, world, local_rank)
+    if line is not None:
+        line.update({"warmup": 1, "vs_baseline": None, "roofline": None, "gpu_launches": None,
+                     "cpu_baseline": None})
         print(json.dumps(line), flush=True)
     return 0
 
@@ -1145,6 +1209,47 @@ def run_gemm(args, rank, world, local_rank):
     return 0
 
 
+def _summary(rec):
+    """The keys of a leg's record that a sub-record keeps."""
+    keep = ("metric", "value", "unit", "steps", "gathers", "ms_per_step", "scaling", "dtype",
+            "roofline", "per_rank", "wall_s", "clocks")
+    out = {k: rec[k] for k in keep if k in rec}
+    out["workload"] = rec["config"]["workload"]
+    if rec.get("e2e"):
+        out["e2e"] = {k: rec["e2e"][k] for k in ("value", "unit") if k in rec["e2e"]}
+    return out
+
+
+def add_subrecords(args, line, rank, world, local_rank):
+    """Run the other configs after the C1 headline; every rank takes part.
+
+    * ``c3``: config 3 (4 x 131072, split-K) through the same fused step,
+      HBM roofline of its launch;
+    * ``prefill``: kernel 3 on the Llama-3-8B attention shape, tensor
+      roofline against the burst bf16 peak;
+    * ``engine_c4``: config 4 (1024 mixed requests) through the
+      sequence-sharded engine with its NCCL token gather: generated tokens/s,
+      steps, gathers and each rank's time in local steps and in the gathers.
+    """
+    import gc
+
+    import torch
+
+    subs = {}
+    for name, fn in (("c3", lambda: decode_leg(args, "c3", rank, world, local_rank, cpu_base=False)),
+                     ("prefill", lambda: prefill_leg(args, "prefill", rank, world, local_rank,
+                                                     cpu_base=False)),
+                     ("engine_c4", lambda: c4_leg(args, rank, world, local_rank))):
+        gc.collect()
+        torch.cuda.empty_cache()
+        rec = fn()
+        if rank == 0:
+            subs[name] = _summary(rec)
+    if rank == 0:
+        line["subrecords"] = subs
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -1155,6 +1260,8 @@ def main():
                     choices=sorted(CONFIGS) + sorted(PREFILL) + sorted(ENGINE) + ["c4", "gemm"],
                     default="c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-subrecords", action="store_true",
+                    help="c1: skip the c3 / prefill / sharded-engine sub-records")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -1174,7 +1281,7 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": why}))
         return 0
     if args.impl == "reference":
-        return run_prefill(args, rank, world, local_rank)
+        return run_prefill_reference(args, rank, world)
     if world > 1:
         import torch
         import torch.distributed as dist
@@ -1190,8 +1297,14 @@ def main():
         if args.config in ENGINE:
             return run_engine(args, rank, world, local_rank)
         if cfg is None:
-            return run_prefill(args, rank, world, local_rank)
-        return run_ours(args, cfg, rank, world, local_rank)
+            line = prefill_leg(args, args.config, rank, world, local_rank)
+        else:
+            line = decode_leg(args, args.config, rank, world, local_rank)
+            if args.config == "c1" and not args.no_subrecords:
+                line = add_subrecords(args, line, rank, world, local_rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -154,23 +154,24 @@ int vmps_paged_decode_step(void* out, void* q, int64_t q_row_stride, const void*
 
 /*
  * Allocation-free variant of vmps_paged_decode_attention.  No counterpart in
- * the reference (whose Metal path keeps a global output buffer instead,
- * kernels/__init__.py:317-345); it exists for callers that cannot allocate
- * device memory while running (a C/FFI host without a caching allocator, or
- * a process that has already reserved all free HBM for its KV pool), which
- * therefore cannot pass the workspace the other entry point needs.
+ * the reference.  It exists for callers that cannot allocate device memory
+ * while running (a C/FFI host without a caching allocator, or a process that
+ * has already reserved all free HBM for its KV pool), which therefore cannot
+ * pass the workspace the other entry point needs.
  *
  * Same arguments and results as vmps_paged_decode_attention minus the
  * workspace: the split-K scratch is a fixed 8 MiB device array inside the
  * library, held on every GPU that loads the library until exit.  Calls that
  * would need more scratch (vmps_paged_decode_workspace_bytes) return
  * VMPS_ERR_WORKSPACE; on a 148-SM B200 every supported shape with up to 8
- * query heads per kv head fits, 16 query heads per kv head does not.  All calls on a device share the array, so calls that
- * may overlap on the GPU race and must be ordered on one stream.  The first
- * call on a device looks up the array's address (cudaGetSymbolAddress),
- * caches it and clears the array on the caller's stream (its merge counters
- * must start at zero; every call leaves them at zero); make that first call
- * before any stream capture.  Allocates nothing (no cudaMalloc/cudaFree).
+ * query heads per kv head fits, 16 query heads per kv head does not.  All calls
+ * on a device share the array, so calls that may overlap on the GPU race and
+ * must be ordered on one stream.  Every call first clears the merge counters
+ * it uses (n_kv * num_seqs ints) with a cudaMemsetAsync on `stream`, so a
+ * call that gave up a bounded wait (error bit 8) cannot disturb the next.
+ * The first call on a device looks up the array's address
+ * (cudaGetSymbolAddress) and caches it; make that first call before any
+ * stream capture.  Allocates nothing (no cudaMalloc/cudaFree).
  */
 int vmps_paged_decode_attention_noalloc(void* out, const void* q, const void* pool,
                                         const int32_t* block_tables, int max_blocks_per_seq,

@@ -88,6 +88,14 @@ constexpr int kMaxKvHeads = 64;
 // in shared memory up front; later segments read them from global memory.
 constexpr int kSegTables = VMPS_DECODE_SEG_TABLES;
 constexpr int kPageTokens = 16;
+// Bytes of its first pages that a CTA pulls into L2 before the PDL wait in
+// the fused step.  296 CTAs x 256 KiB = 74 MiB stays well inside the 126 MB
+// L2 whatever the workload; a C1-sized chunk (~14 pages of 16 KiB) is
+// prefetched whole.
+#ifndef VMPS_DECODE_PREFETCH_BYTES
+#define VMPS_DECODE_PREFETCH_BYTES (256 * 1024)
+#endif
+constexpr int kPrefetchBytes = VMPS_DECODE_PREFETCH_BYTES;
 
 struct DecodeParams {
   void* out;
@@ -391,8 +399,23 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
     // latency (long while the page stream keeps HBM queues full) is hidden.
     int cur_phys = 0, cur_hg = 0;
     if (u_begin + lane < u_end) unit_block(u_begin + lane, cur_hg, cur_phys);
-    // The pool may still be being written by the previous kernel.
-    if (p.early_prologue) pdl_wait();
+    if (p.early_prologue) {
+      // The pool may still be being written by the previous kernel, so pages
+      // go to shared memory only after the PDL wait -- but they can be pulled
+      // into L2 now (L2 is coherent with those writes): the first
+      // kPrefetchUnits pages of this CTA's chunk stream from HBM while the
+      // previous launch drains, and the loads after the wait hit L2.
+      constexpr int kPrefetchUnits =
+          (kPrefetchBytes / Shape::kStageBytes) < 32 ? (kPrefetchBytes / Shape::kStageBytes) : 32;
+      if (lane < kPrefetchUnits && u_begin + lane < u_end && cur_phys >= 0 &&
+          cur_phys < p.num_blocks) {
+#pragma unroll
+        for (int dh = 0; dh < Shape::kDHalves; ++dh) {
+          tma_prefetch_l2_4d(&tmap, dh * 64, 0, cur_hg * HPC, 2 * cur_phys);
+        }
+      }
+      pdl_wait();
+    }
     pdl_trigger();
     if (u_begin >= u_end) return;
     if (lane == 0) prefetch_tmap(&tmap);
@@ -479,6 +502,28 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
     l_slot = p.fused ? p.slot_mapping[sq] : -1;
   }
 
+  if (p.early_prologue) {
+    // The first segments' q rows and new K/V rows into L2 before the wait
+    // (the previous kernel may still be writing them; L2 stays coherent),
+    // so the cp.async staging after the wait hits L2.
+    const int h = warp - 1;
+    const int qbytes = p.G * D * static_cast<int>(sizeof(T));
+    for (int k = 0; k < n_seg; ++k) {
+      const int sq = seg_seq[k];
+      const int kvh = seg_hg[k] * HPC + h;
+      const char* qrow = reinterpret_cast<const char*>(
+          static_cast<const T*>(p.q) + static_cast<size_t>(sq) * p.q_stride +
+          static_cast<size_t>(kvh) * p.G * D);
+      for (int off = lane * 128; off < qbytes; off += 32 * 128) {
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(qrow + off));
+      }
+      if (lane == 31 || lane == 30) {
+        const T* src = lane == 31 ? static_cast<const T*>(p.k) + static_cast<size_t>(sq) * p.k_stride
+                                  : static_cast<const T*>(p.v) + static_cast<size_t>(sq) * p.v_stride;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(src + static_cast<size_t>(kvh) * D));
+      }
+    }
+  }
   // q/k/v and the output may still be in use by the previous kernel.
   if (p.early_prologue) pdl_wait();
   pdl_trigger();
@@ -978,6 +1023,11 @@ static WorkspaceLayout workspace_layout(int num_seqs, int n_kv, int D, const Dec
   w.o = w.ml + align256(recs * cfg.nt * 4 * 4 * sizeof(float));
   w.total = w.o + align256(recs * cfg.nt * (D / 16) * 32 * 4 * sizeof(float));
   return w;
+}
+
+size_t decode_counter_bytes(int num_seqs, int n_kv) {
+  if (num_seqs <= 0 || num_seqs > kMaxSeqs || n_kv <= 0 || n_kv > kMaxKvHeads) return 0;
+  return static_cast<size_t>(num_seqs) * n_kv * sizeof(int);
 }
 
 // Launches `kernel` with programmatic dependent launch enabled, so it may

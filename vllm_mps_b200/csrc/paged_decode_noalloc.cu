@@ -20,16 +20,18 @@
 //     (~6 MB: 1 MiB of merge counters plus the split-K partials of the
 //     grid) and rejects 16 query heads per kv head (~10.8 MB).
 //   * All calls on a device share the array and it keeps the last call's
-//     contents.  Its merge counters must start at zero: the first call on a
-//     device clears the whole array (cudaMemsetAsync on the caller's stream,
-//     not an allocation), and every call leaves the counters at zero again;
-//     the partial results are always written before they are read.  Calls
-//     whose kernels may overlap on the GPU (different streams without
-//     ordering) race on the array and must not be issued.
+//     contents.  The kernel's split-K merge counters must be zero when it
+//     starts.  A call that completes leaves them at zero, but one whose
+//     kernel gave up a bounded wait (error bit 8) can leave some behind, and
+//     the caller has no handle on the array to reset it.  So every call
+//     first clears the counters it will use -- n_kv * num_seqs ints at the
+//     start of the array -- with cudaMemsetAsync on its own stream (a memset,
+//     not an allocation); the partial results are always written before
+//     they are read.  Calls whose kernels may overlap on the GPU (different
+//     streams without ordering) race on the array and must not be issued.
 //   * The first call on a device resolves the array's device address with
-//     cudaGetSymbolAddress (with that device current), caches it and clears
-//     the array; make that first call before any stream capture on the
-//     device.
+//     cudaGetSymbolAddress (with that device current) and caches it; make
+//     that first call before any stream capture on the device.
 //   * Nothing here calls cudaMalloc, cudaFree or any allocating routine.
 #include <mutex>
 
@@ -43,8 +45,8 @@ static __device__ __align__(256) uint8_t g_decode_scratch[kNoAllocScratchBytes];
 
 // Device address of g_decode_scratch on the current device.  The name is a
 // host-side stand-in in host code; only this address may be given to a
-// kernel.  The first use on a device also clears the array on `stream`.
-static int noalloc_scratch(void** out, cudaStream_t stream) {
+// kernel.
+static int noalloc_scratch(void** out) {
   static void* cached[64];
   static int status[64];
   static std::once_flag flags[64];
@@ -54,15 +56,13 @@ static int noalloc_scratch(void** out, cudaStream_t stream) {
   }
   std::call_once(flags[dev], [&] {
     void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
-    if (e == cudaSuccess) e = cudaMemsetAsync(p, 0, kNoAllocScratchBytes, stream);
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
     status[dev] = static_cast<int>(e);
     cached[dev] = (e == cudaSuccess) ? p : nullptr;
   });
   if (!cached[dev]) {
     return fail(VMPS_ERR_CUDA,
-                "paged_decode_attention_noalloc: resolving or clearing the scratch array "
-                "failed: %s",
+                "paged_decode_attention_noalloc: resolving the scratch array failed: %s",
                 cudaGetErrorString(static_cast<cudaError_t>(status[dev])));
   }
   *out = cached[dev];
@@ -99,8 +99,21 @@ extern "C" int vmps_paged_decode_attention_noalloc(void* out, const void* q, con
                 "vmps_paged_decode_attention with a caller-provided workspace)",
                 need, kNoAllocScratchBytes);
   }
+  const size_t counter_bytes = decode_counter_bytes(num_seqs, n_kv);
+  if (counter_bytes == 0) {
+    return fail(VMPS_ERR_UNSUPPORTED,
+                "paged_decode_attention_noalloc: num_seqs=%d n_kv=%d outside the kernel's limits",
+                num_seqs, n_kv);
+  }
   void* scratch = nullptr;
-  if (int rc = noalloc_scratch(&scratch, static_cast<cudaStream_t>(stream))) return rc;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  // Counters left behind by an earlier call that gave up a wait would make
+  // this call skip merges; clear the ones it uses.
+  const cudaError_t e = cudaMemsetAsync(scratch, 0, counter_bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    return fail(VMPS_ERR_CUDA, "paged_decode_attention_noalloc: clearing the merge counters failed: %s",
+                cudaGetErrorString(e));
+  }
   return vmps_paged_decode_attention(out, q, pool, block_tables, max_blocks_per_seq, seq_lens,
                                      num_seqs, n_q, n_kv, head_dim, block_size, num_blocks, scale,
                                      scratch, kNoAllocScratchBytes, dtype, stream);

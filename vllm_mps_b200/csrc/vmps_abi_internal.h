@@ -24,6 +24,11 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, int rank, void* base,
                  const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                  CUtensorMapSwizzle swizzle);
 
+// Bytes at the start of a decode workspace that hold the split-K merge
+// counters one call of this shape uses (n_kv * num_seqs ints), or 0 when the
+// shape is outside what the decode kernel accepts.
+size_t decode_counter_bytes(int num_seqs, int n_kv);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace vmps

@@ -21,6 +21,7 @@ a collective the others never enter.
 from __future__ import annotations
 
 import heapq
+import time
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -102,6 +103,11 @@ class ShardedEngine:
         self._local_to_global: dict[int, int] = {}
         self.outputs: dict[int, ShardedOutput] = {}
         self.steps = 0
+        self.gathers = 0
+        # Host wall time in local engine steps and in the gathers (the
+        # gather's time includes waiting for the slowest rank to arrive).
+        self.step_seconds = 0.0
+        self.gather_seconds = 0.0
         self._rec = 0
         self._send = self._recv = None
 
@@ -143,7 +149,10 @@ class ShardedEngine:
 
         if self._send is None:
             self._size_records([])
+        t0 = time.perf_counter()
         produced = self.engine.step() if not self.engine.is_finished() else []
+        t1 = time.perf_counter()
+        self.step_seconds += t1 - t0
         if len(produced) > self.capacity:
             raise RuntimeError(f"rank {self.rank}: {len(produced)} sequences in one step "
                                f"exceed the record capacity {self.capacity}")
@@ -163,6 +172,8 @@ class ShardedEngine:
         self._send.copy_(torch.from_numpy(rec), non_blocking=False)
         dist.all_gather_into_tensor(self._recv, self._send, group=self.group)
         allrec = self._recv.view(self.world, self._rec).cpu().numpy()
+        self.gathers += 1
+        self.gather_seconds += time.perf_counter() - t1
         more = bool((allrec[:, 0] > 0).any())
         slots = (self._rec - 1) // 3
         for r in range(self.world):
