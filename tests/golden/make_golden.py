@@ -33,6 +33,10 @@ What is captured
   reference engine (engine/llm_engine.py:316-346); tokens plus the top-5
   logits of every decision, and the shared pool's used blocks at the start
   of decisions 5 and 14.  (Needs ~2 min of CPU; ``--skip-engine``.)
+* ``engine_c0_physical.npz`` -- the same model and prompts through the
+  reference's classes with one pool per layer and every prompt token but
+  the last run through the single-token path first (the well-conditioned
+  mode), then 20 greedy steps of the reference engine.
 
 Usage::
 
@@ -592,6 +596,121 @@ def gen_engine_c0(pal):
     print(f"engine_c0: {steps} steps, {tokens.size} tokens in {dt:.2f}s")
 
 
+def gen_engine_c0_physical(pal, steps: int = 20):
+    """Config 0 through the reference classes in the well-conditioned mode.
+
+    The reference engine shares ONE pool across all layers and feeds only
+    the last prompt token (engine/llm_engine.py:166-193, :323-329), which
+    makes its trace chaotic under rounding.  Its layer takes the pool as a
+    constructor argument (layers/paged_attention_layer.py:36-38), so here
+    every layer gets its own ``MPSMemoryPool``; after the first
+    ``Scheduler.schedule()`` has allocated the prompt slots, every prompt
+    token but the last is run through the single-token path
+    (``LlamaAdapter.forward_single_token``, models/llama_adapter.py:112-133 ->
+    ``_forward_single``, layers/paged_attention_layer.py:175-241), in order,
+    so each layer's pool holds the prompt's K/V; then ``steps`` greedy decode
+    steps run through the reference engine (``_step_adapter`` for the
+    first, ``step()`` after it).  Stored: tokens, top-5 logits and ids of
+    every decision.
+    """
+    import torch
+    from transformers import LlamaForCausalLM
+    from vllm_mps.core.kv_cache_manager import KVCacheManager
+    from vllm_mps.core.model_config import ModelConfig
+    from vllm_mps.core.sequence import SamplingParams, Sequence, SequenceGroup
+    from vllm_mps.engine.llm_engine import LLMEngine, RequestOutput
+    from vllm_mps.engine.scheduler import Scheduler
+    from vllm_mps.memory.mps_memory_pool import MPSMemoryPool
+    from vllm_mps.model.sampler import Sampler
+    import vllm_mps.models.llama_adapter as la
+
+    torch.set_num_threads(os.cpu_count())
+    hf_cfg = c0_llama_config()
+    torch.manual_seed(0)
+    model = LlamaForCausalLM(hf_cfg).to(torch.float16).eval()
+    cfg = ModelConfig(
+        model_name="tinyllama-random", architecture="llama", d_model=2048,
+        n_heads=32, n_kv_heads=4, d_k=64, n_layers=22, vocab_size=32000,
+        max_seq_len=2048, rope_theta=10000.0, dtype=torch.float16,
+        device=torch.device("cpu"),
+    )
+    nblocks = 64
+    kv = KVCacheManager(nblocks, 32)
+    pools = [MPSMemoryPool(nblocks, 16, 4, 64, torch.float16, torch.device("cpu"))
+             for _ in model.model.layers]
+    adapter = la.LlamaAdapter("tinyllama-random")
+    adapter.model_config, adapter.kv_cache_manager, adapter.memory_pool = cfg, kv, pools[0]
+    adapter.hf_model = model
+    adapter.paged_layers = []
+    for i, layer in enumerate(model.model.layers):
+        pl = pal.PagedAttentionLayer.from_llama_layer(layer.self_attn, i, cfg, kv, pools[i])
+        layer.self_attn = pl
+        adapter.paged_layers.append(pl)
+
+    eng = LLMEngine.__new__(LLMEngine)
+    eng.memory_pool, eng.kv_cache_manager = pools[0], kv
+    eng.scheduler = Scheduler(kv, max_batch_size=8, max_tokens_per_step=100000)
+    eng.sampler = Sampler()
+    eng.model = eng.model_runner = None
+    eng._request_counter = 0
+    eng._outputs, eng._seq_to_request, eng._seq_to_params = {}, {}, {}
+    eng.total_tokens_generated = 0
+    eng.start_time = time.time()
+    eng.adapter = adapter
+    eng.model_config = cfg
+
+    class _Tok:
+        def decode(self, ids, skip_special_tokens=True):
+            return ""
+
+    eng.tokenizer = _Tok()
+    g = torch.Generator().manual_seed(0)
+    prompts = torch.randint(0, 32000, (8, 32), generator=g).tolist()
+    params = SamplingParams(temperature=0.0, max_tokens=steps)
+    for rid, p in enumerate(prompts):
+        seq = Sequence(rid, "", p, params)
+        eng.scheduler.add_request(SequenceGroup(rid, [seq], params))
+        eng._outputs[rid] = RequestOutput(request_id=rid, prompt="")
+        eng._seq_to_request[rid] = rid
+        eng._seq_to_params[rid] = params
+
+    top_vals, top_ids, step_seqs = [], [], []
+    orig = adapter.forward_batch
+
+    def wrapped(token_ids, seq_ids, positions, seq_lens):
+        logits = orig(token_ids, seq_ids, positions, seq_lens)
+        v, i = torch.topk(logits.float(), 5, dim=-1)
+        top_vals.append(v.numpy())
+        top_ids.append(i.numpy())
+        step_seqs.append(list(seq_ids))
+        return logits
+
+    adapter.forward_batch = wrapped
+    t0 = time.perf_counter()
+    sched_out = eng.scheduler.schedule()  # admits all 8, allocates the prompt slots
+    assert len(sched_out.scheduled_groups) == 8
+    for rid, p in enumerate(prompts):
+        for pos, tok in enumerate(p[:-1]):
+            adapter.forward_single_token(tok, pos, rid)
+    t_prefill = time.perf_counter() - t0
+    eng._step_adapter(sched_out)
+    n = 1
+    while not eng.is_finished():
+        eng.step()
+        n += 1
+    dt = time.perf_counter() - t0
+    tokens = np.array([eng._outputs[r].token_ids for r in range(8)], dtype=np.int64)
+    np.savez_compressed(
+        os.path.join(HERE, "engine_c0_physical.npz"),
+        prompts=np.array(prompts, dtype=np.int64), tokens=tokens,
+        top_vals=np.stack(top_vals), top_ids=np.stack(top_ids),
+        step_seqs=np.array(step_seqs, dtype=np.int64),
+        cpu_seconds=dt, prefill_seconds=t_prefill, cpu_threads=torch.get_num_threads(),
+    )
+    print(f"engine_c0_physical: {n} steps, {tokens.size} tokens in {dt:.1f}s "
+          f"(prefill {t_prefill:.1f}s)")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference source tree")
@@ -615,6 +734,8 @@ def main():
         gen_sched_trace(74, 48, "sched_trace_oom.npz")
     if not a.skip_engine and (not a.only or a.only == "engine"):
         gen_engine_c0(pal)
+    if not a.skip_engine and (not a.only or a.only == "engine_physical"):
+        gen_engine_c0_physical(pal)
 
 
 if __name__ == "__main__":

@@ -124,6 +124,88 @@ def test_c0_greedy_parity_with_reference(c0_model, record_property):
     record_property("c0_chained_top5_deviation", chained)
 
 
+# Physical mode against the reference's classes run in the same mode
+# (tests/golden/engine_c0_physical.npz: one pool per layer, prompts through
+# the single-token path, 20 greedy steps; make_golden.gen_engine_c0_physical).
+# Measured on a B200 (teacher-forced, all 160 decisions): the logits of the
+# reference's top-5 tokens agree within PHYS_LOGIT_TOL.  The reference's
+# logits are fp16 (one ulp = 0.0039 at magnitude 2-4), and its smallest
+# top-1/top-2 margin is one such ulp; a decision whose margin is below twice
+# the logit tolerance may go either way, every other one must agree.
+PHYS_LOGIT_TOL = 0.05
+
+
+def _run_physical_c0(model, forced_tokens=None):
+    from vllm_mps_b200.core.sequence import SamplingParams
+    from vllm_mps_b200.engine.llm_engine import LLMEngine
+
+    d = load_golden("engine_c0_physical.npz")
+    eng = LLMEngine.from_model(model, num_gpu_blocks=256, num_cpu_blocks=32, max_batch_size=8,
+                               max_tokens_per_step=100000, mode="physical",
+                               dtype=torch.float16, device="cuda")
+    seen = []
+    real = eng.sampler.sample_rows
+
+    def spy(logits, params, generator=None):
+        seen.append(logits.float().cpu())
+        if forced_tokens is not None:
+            t = len(seen) - 1
+            return [int(forced_tokens[s][t]) for s in d["step_seqs"][t]]
+        return real(logits, params, generator)
+
+    eng.sampler.sample_rows = spy
+    for p in d["prompts"].tolist():
+        eng.add_request(p, SamplingParams(temperature=0.0, max_tokens=20))
+    while not eng.is_finished():
+        eng.step()
+    return np.array([eng.get_output(r).token_ids for r in range(8)]), seen, d
+
+
+def test_c0_physical_free_running_greedy_parity(c0_model, record_property):
+    """Free-running greedy decode in physical mode against the reference run
+    in the same mode: every sequence's tokens are identical up to its first
+    divergence, and a divergence may only come at a decision the reference
+    itself calls within 2 * PHYS_LOGIT_TOL (top-1 minus top-2 logit)."""
+    ours, seen, d = _run_physical_c0(c0_model)
+    ref, top_vals = d["tokens"], d["top_vals"]
+    margin = top_vals[:, :, 0] - top_vals[:, :, 1]
+    firsts = []
+    for s in range(8):
+        diff = np.flatnonzero(ours[s] != ref[s])
+        if diff.size:
+            t = int(diff[0])
+            firsts.append((s, t, float(margin[t, s])))
+            assert margin[t, s] < 2 * PHYS_LOGIT_TOL, (s, t, float(margin[t, s]))
+    record_property("physical_identical_tokens", int((ours == ref).sum()))
+    record_property("physical_identical_sequences", int(sum((ours[s] == ref[s]).all() for s in range(8))))
+    record_property("physical_first_divergences", firsts)
+
+
+def test_c0_physical_teacher_forced_logits(c0_model, record_property):
+    """Teacher-forced with the reference's tokens, all 20 decisions of all 8
+    sequences: the logits of the reference's top-5 tokens within
+    PHYS_LOGIT_TOL, and the greedy token identical wherever the reference's
+    margin exceeds 2 * PHYS_LOGIT_TOL."""
+    d = load_golden("engine_c0_physical.npz")
+    _, seen, d = _run_physical_c0(c0_model, forced_tokens=d["tokens"])
+    top_vals, top_ids = d["top_vals"], d["top_ids"]
+    assert len(seen) == 20
+    worst, flips = 0.0, []
+    for t in range(20):
+        L = seen[t]
+        dev = (L.gather(1, torch.from_numpy(top_ids[t])) - torch.from_numpy(top_vals[t])).abs().max()
+        worst = max(worst, float(dev))
+        margin = top_vals[t, :, 0] - top_vals[t, :, 1]
+        ours_top = L.argmax(-1).numpy()
+        for row in range(8):
+            if ours_top[row] != top_ids[t, row, 0]:
+                flips.append((t, row, float(margin[row])))
+                assert margin[row] < 2 * PHYS_LOGIT_TOL, (t, row, float(margin[row]))
+    record_property("physical_top5_max_deviation", round(worst, 4))
+    record_property("physical_teacher_forced_flips", flips)
+    assert worst < PHYS_LOGIT_TOL, worst
+
+
 def _small_llama(seed=1, layers=4, heads=8, kv_heads=2, head_dim=64, vocab=1024):
     from transformers import LlamaConfig, LlamaForCausalLM
 

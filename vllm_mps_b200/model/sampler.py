@@ -25,16 +25,47 @@ class Sampler:
         """One token per row with shared parameters (:62-79)."""
         return self.sample_rows(logits_batch, [sampling_params] * logits_batch.size(0))
 
+    @staticmethod
+    def _sorted_filtered(logits: torch.Tensor, params: list[SamplingParams]):
+        """Temperature, top-k and top-p of every row at once, in sorted order.
+
+        Returns (values, order): each row's scaled logits sorted descending
+        with the dropped tokens at -inf, and the vocab index of each column.
+        The reference's per-row steps (model/sampler.py:36-59): divide by
+        the temperature; top-k keeps every logit >= the k-th largest (ties
+        kept); top-p drops sorted tokens whose cumulative probability before
+        them is >= top_p.
+        """
+        dev = logits.device
+        temp = torch.tensor([p.temperature for p in params], device=dev)
+        k = torch.tensor([p.top_k for p in params], device=dev, dtype=torch.long)
+        top_p = torch.tensor([p.top_p for p in params], device=dev)
+        V = logits.size(-1)
+        sv, order = torch.sort(logits.float() / temp[:, None], dim=-1, descending=True)
+        kth = sv.gather(1, (k.clamp(1, V) - 1)[:, None])
+        kth = torch.where((k > 0)[:, None], kth, torch.full_like(kth, float("-inf")))
+        sv = sv.masked_fill(sv < kth, float("-inf"))
+        probs = F.softmax(sv, dim=-1)
+        cum = torch.cumsum(probs, dim=-1)
+        drop = (cum - probs >= top_p[:, None]) & (top_p < 1.0)[:, None]
+        return sv.masked_fill(drop, float("-inf")), order
+
+    def filtered_logits(self, logits: torch.Tensor, params: list[SamplingParams]) -> torch.Tensor:
+        """The logits each row samples from (vocab order, dropped tokens at -inf).
+
+        Every row must have ``temperature > 0``.
+        """
+        if any(p.temperature == 0.0 for p in params):
+            raise ValueError("filtered_logits: greedy rows have no sampling distribution")
+        sv, order = self._sorted_filtered(logits, params)
+        return torch.full_like(sv, float("-inf")).scatter_(1, order, sv)
+
     def sample_rows(self, logits: torch.Tensor, params: list[SamplingParams],
                     generator: torch.Generator | None = None) -> list[int]:
         """One token per row: one argmax for the batch, one batched pass for the rest.
 
-        Rows with ``temperature > 0`` are filtered and sampled together on the
-        device (one sort of those rows): the reference's per-row steps
-        (model/sampler.py:36-59) -- divide by the temperature; top-k keeps
-        every logit >= the k-th largest (ties kept); top-p drops sorted tokens
-        whose cumulative probability before them is >= top_p; sample from the
-        softmax -- evaluated for all rows at once in sorted order.
+        Rows with ``temperature > 0`` are filtered (``_sorted_filtered``) and
+        sampled together on the device from the softmax of what is left.
         """
         B = logits.size(0)
         if B == 0:
@@ -42,20 +73,8 @@ class Sampler:
         out = torch.argmax(logits, dim=-1)
         rows = [i for i, p in enumerate(params) if p.temperature != 0.0]
         if rows:
-            dev = logits.device
-            idx = torch.tensor(rows, device=dev)
-            temp = torch.tensor([params[i].temperature for i in rows], device=dev)
-            k = torch.tensor([params[i].top_k for i in rows], device=dev, dtype=torch.long)
-            top_p = torch.tensor([params[i].top_p for i in rows], device=dev)
-            V = logits.size(-1)
-            sv, order = torch.sort(logits[idx].float() / temp[:, None], dim=-1, descending=True)
-            kth = sv.gather(1, (k.clamp(1, V) - 1)[:, None])
-            kth = torch.where((k > 0)[:, None], kth, torch.full_like(kth, float("-inf")))
-            sv = sv.masked_fill(sv < kth, float("-inf"))
-            probs = F.softmax(sv, dim=-1)
-            cum = torch.cumsum(probs, dim=-1)
-            drop = (cum - probs >= top_p[:, None]) & (top_p < 1.0)[:, None]
-            sv = sv.masked_fill(drop, float("-inf"))
+            idx = torch.tensor(rows, device=logits.device)
+            sv, order = self._sorted_filtered(logits[idx], [params[i] for i in rows])
             pick = torch.multinomial(F.softmax(sv, dim=-1), 1, generator=generator)
             out[idx] = order.gather(1, pick)[:, 0].to(out.dtype)
         return out.tolist()
