@@ -370,16 +370,25 @@ def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
     # rotating), so the timed region is one replay with no graph boundary
     # between steps -- the steady state a serving loop sees.  The warm-up
     # steps are a graph of their own.
+    # The timed graph starts and ends with event-record nodes (external
+    # events), so the events stamp the first launch's start and the last
+    # launch's end on the device; events recorded on the stream around the
+    # replay also see the graph's submission latency, reported beside it.
     graphs = {}
+    ev_in = (torch.cuda.Event(enable_timing=True, external=True),
+             torch.cuda.Event(enable_timing=True, external=True))
 
-    def run_steps(n):
-        if n not in graphs:
-            graphs[n] = capture([lambda i=i: step(i % R) for i in range(n)])
+    def run_steps(n, timed=False):
+        if (n, timed) not in graphs:
+            fns = [lambda i=i: step(i % R) for i in range(n)]
+            if timed:
+                fns = [ev_in[0].record] + fns + [ev_in[1].record]
+            graphs[(n, timed)] = capture(fns)
             torch.cuda.synchronize(dev)
-        graphs[n].replay()
+        graphs[(n, timed)].replay()
 
     run_steps(args.warmup)
-    run_steps(args.steps)
+    run_steps(args.steps, timed=True)
     g_attns = capture([lambda r=r: attn(r) for r in range(R)])
     torch.cuda.synchronize(dev)
     if K.error_word(dev):
@@ -407,11 +416,12 @@ def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index if dev.index is not None else 0) as clocks:
         e0.record()
-        run_steps(args.steps)
+        run_steps(args.steps, timed=True)
         e1.record()
         torch.cuda.synchronize(dev)
     barrier()
-    t_step = max_over_ranks(e0.elapsed_time(e1) * 1e-3)
+    t_step = max_over_ranks(ev_in[0].elapsed_time(ev_in[1]) * 1e-3)
+    t_replay = max_over_ranks(e0.elapsed_time(e1) * 1e-3)
 
     # ── the attention kernel alone (roofline): R launches per graph replay,
     # CUDA events around every replay; duration per launch = replay time / R.
@@ -455,9 +465,10 @@ def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
     packed = [pack(r) for r in range(R)]
     nbytes = packed[0][0].numel()
     offs, sizes = packed[0][1], packed[0][2]
-    stage = [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(2)]
-    douts = [torch.empty((B, n_q, D), dtype=tdt, device=dev) for _ in range(2)]
-    houts = [torch.empty((B, n_q, D), dtype=tdt).pin_memory() for _ in range(2)]
+    NB = 3  # staging buffers: H2D of step i+2 and D2H of step i-1 overlap step i
+    stage = [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(NB)]
+    douts = [torch.empty((B, n_q, D), dtype=tdt, device=dev) for _ in range(NB)]
+    houts = [torch.empty((B, n_q, D), dtype=tdt).pin_memory() for _ in range(NB)]
     maxb_r = tables[0].shape[1]
 
     def views(buf):
@@ -471,27 +482,32 @@ def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
     staged = [views(b) for b in stage]
     s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev = lambda: torch.cuda.Event()  # noqa: E731
-    h2d_done, k_done, d2h_done = [ev(), ev()], [ev(), ev()], [ev(), ev()]
+    h2d_done = [ev() for _ in range(NB)]
+    k_done = [ev() for _ in range(NB)]
+    d2h_done = [ev() for _ in range(NB)]
 
-    def run_pipeline(n):
+    def run_pipeline(n, first=None, last=None):
         comp = torch.cuda.current_stream(dev)
+        if first is not None:
+            first.record(comp)
         for x in (*h2d_done, *k_done, *d2h_done):
             x.record(comp)
 
         def h2d(i):
-            b = i % 2
-            s_h2d.wait_event(k_done[b])  # step i-2 is done with this staging buffer
+            b = i % NB
+            s_h2d.wait_event(k_done[b])  # step i-NB is done with this staging buffer
             with torch.cuda.stream(s_h2d):
                 stage[b].copy_(packed[i % R][0], non_blocking=True)
                 h2d_done[b].record(s_h2d)
 
-        h2d(0)
+        for i in range(min(NB - 1, n)):
+            h2d(i)
         for i in range(n):
-            b = i % 2
-            if i + 1 < n:
-                h2d(i + 1)
+            b = i % NB
+            if i + NB - 1 < n:
+                h2d(i + NB - 1)
             comp.wait_event(h2d_done[b])
-            comp.wait_event(d2h_done[b])  # step i-2's output has left this buffer
+            comp.wait_event(d2h_done[b])  # step i-NB's output has left this buffer
             dq, dk, dv, dpos, dsl, dslot, dbt = staged[b]
             K.paged_decode_step(dq, dk, dv, dpos, dslot, inv, pools[i % R], dbt, dsl,
                                 out=douts[b], workspace=ws)
@@ -500,36 +516,42 @@ def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
             with torch.cuda.stream(s_d2h):
                 houts[b].copy_(douts[b], non_blocking=True)
                 d2h_done[b].record(s_d2h)
-        comp.wait_event(d2h_done[(n - 1) % 2])
-        comp.wait_event(h2d_done[(n - 1) % 2])
+        for b in range(NB):
+            comp.wait_event(d2h_done[b])
+            comp.wait_event(h2d_done[b])
+        if last is not None:
+            last.record(comp)
 
-    # R pipelined steps (one per replica) captured as one CUDA graph with its
-    # copy nodes; every replay moves every step's inputs and output again.
+    # All e2e steps pipelined in ONE CUDA graph with their copy nodes (NB
+    # staging buffers in flight), bracketed by event-record nodes.
+    e2e_steps = args.steps
     with torch.cuda.stream(side):
         run_pipeline(R)
     torch.cuda.synchronize(dev)
-    g_e2e = capture([lambda: run_pipeline(R)])
+    ev_e2e = (torch.cuda.Event(enable_timing=True, external=True),
+              torch.cuda.Event(enable_timing=True, external=True))
+    g_e2e = capture([lambda: run_pipeline(e2e_steps, *ev_e2e)])
+    g_e2e_warm = capture([lambda: run_pipeline(min(e2e_steps, max(args.warmup, NB)))])
     torch.cuda.synchronize(dev)
     # The pipeline computes the same outputs as the device-resident step.
-    K.paged_decode_step(qs[R - 1], k, v, pos, slots[R - 1], inv, pools[R - 1], bts[R - 1], sl,
-                        out=outs[0], workspace=ws)
+    last_i = e2e_steps - 1
+    K.paged_decode_step(qs[last_i % R], k, v, pos, slots[last_i % R], inv, pools[last_i % R],
+                        bts[last_i % R], sl, out=outs[0], workspace=ws)
     torch.cuda.synchronize(dev)
     g_e2e.replay()
     torch.cuda.synchronize(dev)
-    if not torch.equal(houts[(R - 1) % 2], outs[0].cpu()):
+    if not torch.equal(houts[last_i % NB], outs[0].cpu()):
         raise RuntimeError("pipelined end-to-end output differs from the device-resident step")
-    e2e_steps = max(1, args.steps // R) * R
-    for _ in range(max(args.warmup // R, 3)):
-        g_e2e.replay()
+    g_e2e_warm.replay()
     barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record()
-    for _ in range(e2e_steps // R):
-        g_e2e.replay()
+    g_e2e.replay()
     e3.record()
     torch.cuda.synchronize(dev)
     barrier()
-    t_e2e = max_over_ranks(e2.elapsed_time(e3) * 1e-3)
+    t_e2e = max_over_ranks(ev_e2e[0].elapsed_time(ev_e2e[1]) * 1e-3)
+    t_e2e_replay = max_over_ranks(e2.elapsed_time(e3) * 1e-3)
     h2d_bytes = sum(sizes)
     d2h = houts[0].numel() * houts[0].element_size()
     err = K.error_word(dev)
@@ -554,15 +576,18 @@ def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
             "method": {
                 "l2": f"inputs larger than L2: {R} pool/table replicas rotated "
                       f"({R} x {ab / 1e6:.0f} MB touched per cycle)",
-                "timing": f"one CUDA graph of the {args.steps} timed steps (PDL-chained), CUDA "
-                          "events, max over ranks",
+                "timing": f"one CUDA graph of the {args.steps} timed steps (PDL-chained) "
+                          "between two event-record nodes, max over ranks",
+                "replay_us_incl_submission": t_replay * 1e6,
             },
             "e2e": {"value": world * B * e2e_steps / t_e2e, "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps,
                     "api": "vllm_mps_b200.kernels.paged_decode_step; per step one H2D of the "
                            "packed pinned inputs and one D2H of the output, pipelined on two "
-                           f"copy streams, CUDA graphs of {R} steps with their copy nodes"},
+                           f"copy streams ({NB} staging buffers), all steps in one CUDA graph "
+                           "with their copy nodes between two event-record nodes",
+                    "replay_us_incl_submission": t_e2e_replay * 1e6},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profile_traffic(cfg_name),
                          "peak_kind": peak_kind,

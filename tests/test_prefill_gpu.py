@@ -145,6 +145,10 @@ CASES = [
     (4, 4, 64, torch.float16, [(0, 260), (129, 128)], 1e4),
     (16, 8, 128, torch.float16, [(17, 129), (0, 1)], 1e4),
     (64, 8, 128, torch.float16, [(0, 200), (2048, 33)], 1e4),
+    # A CTA holds two 128-row Q tiles: here the first needs one 128-key tile
+    # fewer than the second, and the last CTAs hold a single partial tile.
+    (8, 8, 64, torch.float16, [(100, 300), (0, 129), (7, 128)], 1e4),
+    (16, 8, 128, torch.bfloat16, [(250, 700), (0, 64)], 5e5),
 ]
 
 

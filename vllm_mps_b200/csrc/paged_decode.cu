@@ -60,6 +60,13 @@
 #ifndef VMPS_DECODE_CTAS_PER_SM
 #define VMPS_DECODE_CTAS_PER_SM 2
 #endif
+// CTAs the kernel is compiled to fit on one SM at once (registers and shared
+// memory).  Above VMPS_DECODE_CTAS_PER_SM, CTAs of the next PDL-chained
+// launch can be resident beside this launch's and start their L2 prefetch
+// while it still runs.
+#ifndef VMPS_DECODE_RESIDENT
+#define VMPS_DECODE_RESIDENT VMPS_DECODE_CTAS_PER_SM
+#endif
 
 namespace vmps {
 
@@ -96,6 +103,12 @@ constexpr int kPageTokens = 16;
 #define VMPS_DECODE_PREFETCH_BYTES (256 * 1024)
 #endif
 constexpr int kPrefetchBytes = VMPS_DECODE_PREFETCH_BYTES;
+// 1: a CTA lets the next launch in the stream start before its own PDL wait
+// (the next launch's CTAs then wait for this one to finish, as always).
+#ifndef VMPS_DECODE_EARLY_TRIGGER
+#define VMPS_DECODE_EARLY_TRIGGER 0
+#endif
+constexpr bool kEarlyTrigger = VMPS_DECODE_EARLY_TRIGGER != 0;
 
 struct DecodeParams {
   void* out;
@@ -248,7 +261,7 @@ __device__ __forceinline__ void unpack2(uint32_t w, float& a, float& b) {
 }
 
 template <typename T, int D, int HPC, int NT>
-__global__ void __launch_bounds__(DecodeShape<D, HPC>::kThreads, kCtasPerSm)
+__global__ void __launch_bounds__(DecodeShape<D, HPC>::kThreads, VMPS_DECODE_RESIDENT)
 paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
   using Shape = DecodeShape<D, HPC>;
   constexpr int KS = D / 16;  // k-steps over head_dim, and m-tiles of O^T
@@ -399,6 +412,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
     // latency (long while the page stream keeps HBM queues full) is hidden.
     int cur_phys = 0, cur_hg = 0;
     if (u_begin + lane < u_end) unit_block(u_begin + lane, cur_hg, cur_phys);
+    if (kEarlyTrigger) pdl_trigger();
     if (p.early_prologue) {
       // The pool may still be being written by the previous kernel, so pages
       // go to shared memory only after the PDL wait -- but they can be pulled
@@ -416,7 +430,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
       }
       pdl_wait();
     }
-    pdl_trigger();
+    if (!kEarlyTrigger) pdl_trigger();
     if (u_begin >= u_end) return;
     if (lane == 0) prefetch_tmap(&tmap);
     int it = 0;
@@ -525,8 +539,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
     }
   }
   // q/k/v and the output may still be in use by the previous kernel.
+  if (kEarlyTrigger) pdl_trigger();
   if (p.early_prologue) pdl_wait();
-  pdl_trigger();
+  if (!kEarlyTrigger) pdl_trigger();
   {
     // Stage this warp's kv-head rows of the first segments: the G query rows
     // and, in fused mode, the new token's K and V.

@@ -42,6 +42,11 @@
 #include "vmps_abi_internal.h"
 #include "vmps_common.cuh"
 
+// 1: the pair kernel (two Q tiles per CTA); 0: one Q tile per CTA, two CTAs per SM.
+#ifndef VMPS_PREFILL_PAIR
+#define VMPS_PREFILL_PAIR 0
+#endif
+
 namespace vmps {
 namespace {
 
@@ -550,6 +555,445 @@ int launch_prefill(const CUtensorMap& kv_map, const CUtensorMap& q_map, const Pr
   return check_launch("paged_prefill_attention");
 }
 
+// ── kernel 3, pair form: two 128-row Q tiles per CTA sharing every K/V tile ──
+//
+// One CTA per SM (>= half of its shared memory, all 512 TMEM columns):
+//   TMEM  [0,128) S0 | [128,256) S1 | O0 (D columns) | O1 (D columns)
+//   smem  Q0 | Q1 | K ring (2 x 128 keys) | V ring (2 x 128 keys)
+// The rows of Q tile 1 are the 128 rows after those of Q tile 0 (the next
+// 128/G tokens of the same sequence and kv head), so one K/V load serves 256
+// rows.  Warps 0-3 run the softmax of Q tile 0, warps 4-7 that of Q tile 1
+// (row = TMEM lane), warp 8 loads Q and K, warp 9 loads V, warp 10 (one lane)
+// issues the MMAs (warp 11 idles) in the order
+//   QK0(0) QK1(0) | PV0(j) QK0(j+1) PV1(j) QK1(j+1) | ...
+// so that while one softmax warpgroup works on its S tile the tensor cores
+// run the other tile's PV and next QK.  A key tile is 128 keys (8 pages):
+// with N = 128 a QK MMA reads as many operand bytes per FLOP from shared
+// memory as the SM can deliver, where N = 64 could not.
+constexpr int kPpKeys = 128;
+constexpr int kPpPages = kPpKeys / 16;
+constexpr int kPpStages = 2;
+constexpr int kPpThreads = 384;  // three warpgroups
+constexpr int kPpKWarp = 8;
+constexpr int kPpVWarp = 9;
+constexpr int kPpMmaWarp = 10;      // warp 11 only completes the third warpgroup
+// Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64,512),
+// the load/MMA warpgroup gives up to 48 and the two softmax warpgroups take
+// 224 (256 x 224 + 128 x 48 = 63,488 <= 64,512), so a softmax thread holds
+// its whole 128-key row of S in registers.
+constexpr int kPpRegsSoftmax = 224;
+constexpr int kPpRegsOther = 48;
+constexpr int kPpKRegion = kPpKeys * 128;  // one 64-column chunk of a key tile
+
+template <int D>
+struct PairShape {
+  static constexpr int kChunks = D / 64;
+  static constexpr int kQBytes = kChunks * kRegion;        // one 128-row Q tile
+  static constexpr int kTileBytes = kChunks * kPpKRegion;  // K (or V) of one key tile
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemUsed = 2 * kQBytes + 2 * kPpStages * kTileBytes + kBarBytes;
+  // At least half an SM's shared memory: a second CTA placed beside this one
+  // would only wait for the TMEM columns this one holds.
+  static constexpr int kSmemBytes = kSmemUsed > 118 * 1024 ? kSmemUsed : 118 * 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  // TMEM column of S_t and of O_t.
+  static __device__ __forceinline__ uint32_t col_s(int t) { return t ? kPpKeys : 0u; }
+  static __device__ __forceinline__ uint32_t col_o(int t) { return 2u * kPpKeys + (t ? D : 0u); }
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kPpThreads, 1)
+    paged_prefill_pair_kernel(const __grid_constant__ CUtensorMap kv_map,
+                              const __grid_constant__ CUtensorMap q_map, const PrefillParams p) {
+  using Shape = PairShape<D>;
+  constexpr int KEYS = kPpKeys;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023u) {
+    if (threadIdx.x == 0) set_error(p.err, kDevErrTimeout);
+    return;
+  }
+  uint8_t* sQ = smem_raw;                            // Q0 | Q1
+  uint8_t* sK = sQ + 2 * Shape::kQBytes;             // K ring
+  uint8_t* sV = sK + kPpStages * Shape::kTileBytes;  // V ring
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kPpStages * Shape::kTileBytes);
+  uint64_t* q_full = bars + 0;
+  uint64_t* s_full = bars + 1;   // [2] MMA -> softmax t: S_t(j) in TMEM
+  uint64_t* p_full = bars + 3;   // [2] softmax t -> MMA: P_t(j) written, O_t rescaled
+  uint64_t* o_ready = bars + 5;  // [2] MMA -> softmax t: PV_t(j) complete
+  uint64_t* o_done = bars + 7;   // every MMA complete
+  uint64_t* k_full = bars + 8;   // [kPpStages]
+  uint64_t* k_empty = k_full + kPpStages;
+  uint64_t* v_full = k_empty + kPpStages;
+  uint64_t* v_empty = v_full + kPpStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_empty + kPpStages);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int seq = blockIdx.z;
+  const int kvh = blockIdx.y;
+  const int pair = gridDim.x - 1 - blockIdx.x;  // the longest (last) pairs start first
+  const int q_len = p.q_lens[seq];
+  const int tpt = p.tokens_per_tile;
+  const int tok0 = pair * 2 * tpt;  // first token of Q tile 0
+  if (tok0 >= q_len) return;        // uniform across the CTA, before any barrier
+  const int q_start = p.q_start[seq];
+  const int row0 = p.cu_q[seq];
+  if (q_start < 0 || row0 < 0 || static_cast<long long>(row0) + q_len > p.total_q) {
+    if (threadIdx.x == 0) set_error(p.err, kDevErrQueryRange);
+    return;
+  }
+  if (threadIdx.x == 0 && pair == 0 && kvh == 0 && q_len > p.max_q_len) {
+    set_error(p.err, kDevErrQueryRange);
+  }
+  const bool has1 = tok0 + tpt < q_len;  // Q tile 1 holds at least one row
+  const int tok_end0 = min(q_len, tok0 + tpt);
+  const int tok_end1 = min(q_len, tok0 + 2 * tpt);
+  const int n_tiles0 = (q_start + tok_end0 + KEYS - 1) / KEYS;
+  const int n_tiles1 = has1 ? (q_start + tok_end1 + KEYS - 1) / KEYS : 0;
+  const int n_tiles = has1 ? n_tiles1 : n_tiles0;
+  const int n_keys = q_start + (has1 ? tok_end1 : tok_end0);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full + t, 1);
+      mbar_init(p_full + t, 4);
+      mbar_init(o_ready + t, 1);
+    }
+    mbar_init(o_done, 1);
+    for (int s = 0; s < kPpStages; ++s) {
+      mbar_init(k_full + s, 1);
+      mbar_init(k_empty + s, 1);
+      mbar_init(v_full + s, 1);
+      mbar_init(v_empty + s, 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kPpMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(Shape::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  // Each role's code sits inside the branch that sets its register budget
+  // (no path joins the two before the final barrier), so the compiler can
+  // allocate the softmax code with the larger budget.
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPpRegsOther));
+    if (warp == kPpKWarp || warp == kPpVWarp) {
+      // ── loads: Q0/Q1 and the K tiles on one warp, the V tiles on another;
+      // block ids 32 pages at a time, the next batch fetched a batch ahead.
+      const bool is_v = warp == kPpVWarp;
+      if (!is_v && lane == 0) {
+        prefetch_tmap(&q_map);
+        mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * Shape::kQBytes);
+        for (int t = 0; t < (has1 ? 2 : 1); ++t) {
+  #pragma unroll
+          for (int c = 0; c < Shape::kChunks; ++c) {
+            tma_load_3d(sQ + t * Shape::kQBytes + c * kRegion, &q_map, q_full, c * 64, kvh * p.G,
+                        row0 + tok0 + t * tpt);
+          }
+        }
+      }
+      if (lane == 0) prefetch_tmap(&kv_map);
+      const int32_t* table = p.block_tables + static_cast<size_t>(seq) * p.max_blocks;
+      const int n_pages = (n_keys + 15) >> 4;
+      const int oob = 2 * p.num_blocks;  // past the pool: the TMA fills zeros
+      auto fetch = [&](int page) -> int {  // block id of `page`, or -1
+        if (page >= n_pages) return -1;
+        if (page >= p.max_blocks) {
+          set_error(p.err, kDevErrSeqLen);
+          return -1;
+        }
+        const int b = table[page];
+        if (b < 0 || b >= p.num_blocks) {
+          set_error(p.err, kDevErrBlockRange);
+          return -1;
+        }
+        return b;
+      };
+      int ids = fetch(lane), nxt = fetch(32 + lane), batch = 0;
+      uint64_t* full = is_v ? v_full : k_full;
+      uint64_t* empty = is_v ? v_empty : k_empty;
+      uint8_t* ring = is_v ? sV : sK;
+      int issued = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int page0 = j * kPpPages;
+        if ((page0 >> 5) != batch) {
+          batch = page0 >> 5;
+          ids = nxt;
+          nxt = fetch((batch + 1) * 32 + lane);
+        }
+        int blk[kPpPages];
+  #pragma unroll
+        for (int pg = 0; pg < kPpPages; ++pg) blk[pg] = __shfl_sync(0xffffffffu, ids, (page0 + pg) & 31);
+        bool go = true;
+        if (lane == 0) {
+          const int st = j % kPpStages;
+          if (j >= kPpStages &&
+              (!mbar_wait(empty + st, ((j / kPpStages) - 1) & 1, p.err) || aborted(abort_flag))) {
+            *abort_flag = 1;
+            go = false;
+          } else {
+            mbar_arrive_expect_tx(full + st, Shape::kTileBytes);
+  #pragma unroll
+            for (int pg = 0; pg < kPpPages; ++pg) {
+              const int coord = blk[pg] < 0 ? oob : 2 * blk[pg] + (is_v ? 1 : 0);
+  #pragma unroll
+              for (int c = 0; c < Shape::kChunks; ++c) {
+                tma_load_4d(ring + st * Shape::kTileBytes + c * kPpKRegion + pg * 2048, &kv_map,
+                            full + st, c * 64, 0, kvh, coord);
+              }
+            }
+            issued = j + 1;
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, go ? 1 : 0, 0)) break;
+      }
+      if (lane == 0 && aborted(abort_flag)) {
+        // Let this warp's own loads land before the shared memory is released.
+        if (!is_v) mbar_wait(q_full, 0, p.err);
+        for (int j = max(0, issued - kPpStages); j < issued; ++j) {
+          mbar_wait(full + (j % kPpStages), (j / kPpStages) & 1, p.err);
+        }
+      }
+    } else if (warp == kPpMmaWarp) {
+      // ── MMA issue (one lane) ─────────────────────────────────────────────────
+      if (lane == 0) {
+        const uint32_t idesc_qk = f16_idesc<T>(KEYS, false);
+        const uint32_t idesc_pv = f16_idesc<T>(D, true);
+        auto wait_ring = [&](uint64_t* full, int j) -> bool {
+          if (!mbar_wait(full + (j % kPpStages), (j / kPpStages) & 1, p.err) || aborted(abort_flag)) {
+            return false;
+          }
+          tc_fence_after();
+          return true;
+        };
+        auto qk = [&](int t, int j) {  // S_t = Q_t K(j)^T
+          const uint32_t q_addr = smem_u32(sQ + t * Shape::kQBytes);
+          const uint32_t k_addr = smem_u32(sK + (j % kPpStages) * Shape::kTileBytes);
+          const uint32_t t_s = tmem_base + Shape::col_s(t);
+  #pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint64_t a = sw128_desc(q_addr + (k >> 2) * kRegion + (k & 3) * 32, 16, 1024);
+            const uint64_t b = sw128_desc(k_addr + (k >> 2) * kPpKRegion + (k & 3) * 32, 16, 1024);
+            tc_mma(t_s, a, b, idesc_qk, k > 0 ? 1u : 0u);
+          }
+          tc_commit(s_full + t);
+        };
+        auto pv = [&](int t, int j) {  // O_t += P_t(j) V(j), P_t read from TMEM where S_t was
+          const uint32_t v_addr = smem_u32(sV + (j % kPpStages) * Shape::kTileBytes);
+          const uint32_t t_p = tmem_base + Shape::col_s(t);
+          const uint32_t t_o = tmem_base + Shape::col_o(t);
+  #pragma unroll
+          for (int k = 0; k < KEYS / 16; ++k) {
+            const uint64_t b = sw128_desc(v_addr + k * 2048, kPpKRegion, 1024);
+            tc_mma_ts(t_o, t_p + k * 8, b, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(o_ready + t);
+        };
+        bool ok = mbar_wait(q_full, 0, p.err) && !aborted(abort_flag) && wait_ring(k_full, 0);
+        if (ok) {
+          qk(0, 0);
+          if (has1) qk(1, 0);
+          tc_commit(k_empty + 0);
+        }
+        for (int j = 0; ok && j < n_tiles; ++j) {
+          bool v_in = false;
+          if (j < n_tiles0) {
+            ok = mbar_wait(p_full + 0, j & 1, p.err) && !aborted(abort_flag) && wait_ring(v_full, j);
+            if (!ok) break;
+            v_in = true;
+            pv(0, j);
+          }
+          const bool next = j + 1 < n_tiles;
+          if (next && !(ok = wait_ring(k_full, j + 1))) break;
+          if (j + 1 < n_tiles0) qk(0, j + 1);
+          if (has1 && j < n_tiles1) {
+            ok = mbar_wait(p_full + 1, j & 1, p.err) && !aborted(abort_flag) &&
+                 (v_in || wait_ring(v_full, j));
+            if (!ok) break;
+            tc_fence_after();
+            pv(1, j);
+          }
+          tc_commit(v_empty + (j % kPpStages));
+          if (has1 && j + 1 < n_tiles1) qk(1, j + 1);
+          if (next) tc_commit(k_empty + ((j + 1) % kPpStages));
+        }
+        if (!ok) *abort_flag = 1;
+        // Whatever happened, every MMA this lane issued completes before the
+        // TMEM is freed: o_done fires after all of them.
+        tc_commit(o_done);
+        mbar_wait(o_done, 0, p.err);
+      }
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPpRegsSoftmax));
+    // ── softmax and epilogue of Q tile t: one row per thread ─────────────────
+    const int t = warp >> 2;
+    const int m = threadIdx.x & 127;  // row = TMEM lane
+    const int my_tiles = t ? n_tiles1 : n_tiles0;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem_base + lane_base + Shape::col_s(t);
+    const uint32_t t_o = tmem_base + lane_base + Shape::col_o(t);
+    const int tok_base = tok0 + t * tpt;
+    const int tk = m >> p.g_shift;
+    const int row_pos = q_start + tok_base + tk;
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < my_tiles; ++j) {
+      ok = mbar_wait(s_full + t, j & 1, p.err);
+      ok = __all_sync(0xffffffffu, ok) && !aborted(abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t s[KEYS / 16][16];
+#pragma unroll
+      for (int c = 0; c < KEYS / 16; ++c) tmem_ld16(t_s + c * 16, s[c]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < KEYS / 16; ++c) tmem_ld_fence_regs(s[c]);
+      const int key0 = j * KEYS;
+      // Max on raw scores (the scale is positive), the scale folded into the
+      // exp2 argument; keys past the row's position are -inf.  The warp takes
+      // the masked path together whenever any of its rows needs it.
+      const bool needs_mask = __any_sync(0xffffffffu, key0 + KEYS - 1 > row_pos);
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (needs_mask) {
+#pragma unroll
+        for (int c = 0; c < KEYS / 16; ++c) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (key0 + c * 16 + i > row_pos) s[c][i] = __float_as_uint(-INFINITY);
+            mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(s[c][i]));
+          }
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < KEYS / 16; ++c) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(s[c][i]));
+        }
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
+      const float m_new = fmaxf(m_run, mx);
+      if (j == 0) {
+        m_run = m_new;
+      } else if (__any_sync(0xffffffffu, m_new > m_run + 8.f)) {
+        // Rescale this warp's O rows once PV_t(j - 1) has landed (only it can
+        // have completed since the last wait, so the parity is unambiguous).
+        ok = mbar_wait(o_ready + t, (j - 1) & 1, p.err);
+        ok = __all_sync(0xffffffffu, ok) && !aborted(abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const float alpha = fast_exp2(m_run - m_new);
+#pragma unroll
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t o[16];
+          tmem_ld16(t_o + c * 16, o);
+          tmem_ld_wait();
+          tmem_ld_fence_regs(o);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st16(t_o + c * 16, o);
+        }
+        l_run *= alpha;
+        m_run = m_new;
+      }
+      // P = exp2(s * scale - m) as 16-bit pairs over the first KEYS/2 columns
+      // of this S tile (the A operand of PV in TMEM), 32 keys per store.
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c2 = 0; c2 < KEYS / 32; ++c2) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float a =
+                fast_exp2(fmaf(__uint_as_float(s[2 * c2 + h][2 * i]), p.scale_log2, -m_run));
+            const float b =
+                fast_exp2(fmaf(__uint_as_float(s[2 * c2 + h][2 * i + 1]), p.scale_log2, -m_run));
+            sum4[i & 3] += a + b;
+            pk[h * 8 + i] = Elt<T>::pack(a, b);
+          }
+        }
+        tmem_st16(t_s + c2 * 16, pk);
+      }
+      tmem_st_wait();
+      l_run += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full + t);
+    }
+    // Epilogue: O / l for the rows of this sequence.
+    if (my_tiles > 0) {
+      bool done = ok && mbar_wait(o_done, 0, p.err);
+      done = __all_sync(0xffffffffu, done) && !aborted(abort_flag);
+      if (done) {
+        tc_fence_after();
+        const float inv_l = 1.f / l_run;
+        const bool valid = tok_base + tk < q_len;
+        T* orow = static_cast<T*>(p.out) +
+                  (static_cast<size_t>(row0 + tok_base + tk) * p.n_q + kvh * p.G +
+                   (m & (p.G - 1))) * D;
+#pragma unroll
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t o[16];
+          tmem_ld16(t_o + c * 16, o);
+          tmem_ld_wait();
+          tmem_ld_fence_regs(o);
+          uint32_t packed[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            packed[i] = Elt<T>::pack(__uint_as_float(o[2 * i]) * inv_l,
+                                     __uint_as_float(o[2 * i + 1]) * inv_l);
+          }
+          if (valid) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 16);
+            dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+          }
+        }
+      } else {
+        *abort_flag = 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kPpMmaWarp) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(Shape::kTmemCols)
+                 : "memory");
+  }
+}
+
+template <typename T, int D>
+int launch_prefill_pair(const CUtensorMap& kv_map, const CUtensorMap& q_map,
+                        const PrefillParams& p, dim3 grid, cudaStream_t s) {
+  using Shape = PairShape<D>;
+  static std::once_flag flags[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(VMPS_ERR_CUDA, "device index %d", dev);
+  std::call_once(flags[dev], [] {
+    cudaFuncSetAttribute(paged_prefill_pair_kernel<T, D>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmemBytes);
+  });
+  paged_prefill_pair_kernel<T, D><<<grid, kPpThreads, Shape::kSmemBytes, s>>>(kv_map, q_map, p);
+  return check_launch("paged_prefill_attention");
+}
+
 }  // namespace
 }  // namespace vmps
 
@@ -652,9 +1096,19 @@ extern "C" int vmps_paged_prefill_attention(
   p.tokens_per_tile = tpt;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
-  const dim3 grid((max_q_len + tpt - 1) / tpt, n_kv, num_seqs);
-  if (grid.x > 0x7fffffffu) return fail(VMPS_ERR_UNSUPPORTED, "%s: grid too large", what);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+#if VMPS_PREFILL_PAIR
+  {
+    const dim3 grid((max_q_len + 2 * tpt - 1) / (2 * tpt), n_kv, num_seqs);
+    if (dtype == VMPS_DTYPE_F16) {
+      return head_dim == 64 ? launch_prefill_pair<__half, 64>(kv_map, q_map, p, grid, s)
+                            : launch_prefill_pair<__half, 128>(kv_map, q_map, p, grid, s);
+    }
+    return head_dim == 64 ? launch_prefill_pair<__nv_bfloat16, 64>(kv_map, q_map, p, grid, s)
+                          : launch_prefill_pair<__nv_bfloat16, 128>(kv_map, q_map, p, grid, s);
+  }
+#endif
+  const dim3 grid((max_q_len + tpt - 1) / tpt, n_kv, num_seqs);
   if (dtype == VMPS_DTYPE_F16) {
     return head_dim == 64 ? launch_prefill<__half, 64>(kv_map, q_map, p, grid, s)
                           : launch_prefill<__half, 128>(kv_map, q_map, p, grid, s);
