@@ -465,10 +465,21 @@ def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
     packed = [pack(r) for r in range(R)]
     nbytes = packed[0][0].numel()
     offs, sizes = packed[0][1], packed[0][2]
-    NB = 3  # staging buffers: H2D of step i+2 and D2H of step i-1 overlap step i
-    stage = [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(NB)]
-    douts = [torch.empty((B, n_q, D), dtype=tdt, device=dev) for _ in range(NB)]
-    houts = [torch.empty((B, n_q, D), dtype=tdt).pin_memory() for _ in range(NB)]
+    # Per step: the packed pinned inputs go to a device staging buffer with
+    # kernels.stage_copy -- a kernel that is a link of the decode steps'
+    # programmatic-dependent-launch chain, so it overlaps the step before it
+    # and no copy-engine node ever feeds a decode step (which would cost that
+    # step its early launch) -- then the decode step, then a copy-engine D2H
+    # of the step's output on a copy stream.  Every step writes its own
+    # device output buffer, so the chain never waits for a D2H.
+    # Step i+1's inputs are staged right BEFORE step i's decode kernel: the
+    # fused step reads its lengths and block tables before its PDL wait, so
+    # the kernel just ahead of it must not be the one writing them (three
+    # staging buffers keep the copy clear of the two steps around it).
+    e2e_steps = min(args.steps, 512)
+    stage = [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(3)]
+    douts = [torch.empty((B, n_q, D), dtype=tdt, device=dev) for _ in range(e2e_steps)]
+    houts = [torch.empty((B, n_q, D), dtype=tdt).pin_memory() for _ in range(2)]
     maxb_r = tables[0].shape[1]
 
     def views(buf):
@@ -480,58 +491,41 @@ def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
                 sl(6).view(torch.int32).view(B, maxb_r))
 
     staged = [views(b) for b in stage]
-    s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ev = lambda: torch.cuda.Event()  # noqa: E731
-    h2d_done = [ev() for _ in range(NB)]
-    k_done = [ev() for _ in range(NB)]
-    d2h_done = [ev() for _ in range(NB)]
+    s_d2h = torch.cuda.Stream(dev)
+    k_done = [torch.cuda.Event() for _ in range(2)]
 
     def run_pipeline(n, first=None, last=None):
         comp = torch.cuda.current_stream(dev)
         if first is not None:
             first.record(comp)
-        for x in (*h2d_done, *k_done, *d2h_done):
-            x.record(comp)
-
-        def h2d(i):
-            b = i % NB
-            s_h2d.wait_event(k_done[b])  # step i-NB is done with this staging buffer
-            with torch.cuda.stream(s_h2d):
-                stage[b].copy_(packed[i % R][0], non_blocking=True)
-                h2d_done[b].record(s_h2d)
-
-        for i in range(min(NB - 1, n)):
-            h2d(i)
+        # The first step's inputs go by copy engine (a full dependency): a
+        # stage copy lets the next launch start at once, so two adjacent
+        # stage copies would not order step 0's inputs before it starts.
+        stage[0].copy_(packed[0][0], non_blocking=True)
         for i in range(n):
-            b = i % NB
-            if i + NB - 1 < n:
-                h2d(i + NB - 1)
-            comp.wait_event(h2d_done[b])
-            comp.wait_event(d2h_done[b])  # step i-NB's output has left this buffer
-            dq, dk, dv, dpos, dsl, dslot, dbt = staged[b]
+            if i + 1 < n:
+                K.stage_copy(stage[(i + 1) % 3], packed[(i + 1) % R][0])
+            dq, dk, dv, dpos, dsl, dslot, dbt = staged[i % 3]
             K.paged_decode_step(dq, dk, dv, dpos, dslot, inv, pools[i % R], dbt, dsl,
-                                out=douts[b], workspace=ws)
+                                out=douts[i], workspace=ws)
+            b = i % 2
             k_done[b].record(comp)
             s_d2h.wait_event(k_done[b])
             with torch.cuda.stream(s_d2h):
-                houts[b].copy_(douts[b], non_blocking=True)
-                d2h_done[b].record(s_d2h)
-        for b in range(NB):
-            comp.wait_event(d2h_done[b])
-            comp.wait_event(h2d_done[b])
+                houts[b].copy_(douts[i], non_blocking=True)
+        comp.wait_stream(s_d2h)
         if last is not None:
             last.record(comp)
 
-    # All e2e steps pipelined in ONE CUDA graph with their copy nodes (NB
-    # staging buffers in flight), bracketed by event-record nodes.
-    e2e_steps = args.steps
+    # All e2e steps in ONE CUDA graph with their copies, bracketed by
+    # event-record nodes.
     with torch.cuda.stream(side):
-        run_pipeline(R)
+        run_pipeline(min(e2e_steps, R))
     torch.cuda.synchronize(dev)
     ev_e2e = (torch.cuda.Event(enable_timing=True, external=True),
               torch.cuda.Event(enable_timing=True, external=True))
     g_e2e = capture([lambda: run_pipeline(e2e_steps, *ev_e2e)])
-    g_e2e_warm = capture([lambda: run_pipeline(min(e2e_steps, max(args.warmup, NB)))])
+    g_e2e_warm = capture([lambda: run_pipeline(min(e2e_steps, max(args.warmup, 2)))])
     torch.cuda.synchronize(dev)
     # The pipeline computes the same outputs as the device-resident step.
     last_i = e2e_steps - 1
@@ -540,7 +534,7 @@ def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
     torch.cuda.synchronize(dev)
     g_e2e.replay()
     torch.cuda.synchronize(dev)
-    if not torch.equal(houts[last_i % NB], outs[0].cpu()):
+    if not torch.equal(houts[last_i % 2], outs[0].cpu()):
         raise RuntimeError("pipelined end-to-end output differs from the device-resident step")
     g_e2e_warm.replay()
     barrier()
@@ -583,10 +577,10 @@ def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
             "e2e": {"value": world * B * e2e_steps / t_e2e, "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps,
-                    "api": "vllm_mps_b200.kernels.paged_decode_step; per step one H2D of the "
-                           "packed pinned inputs and one D2H of the output, pipelined on two "
-                           f"copy streams ({NB} staging buffers), all steps in one CUDA graph "
-                           "with their copy nodes between two event-record nodes",
+                    "api": "vllm_mps_b200.kernels.stage_copy (packed pinned inputs -> device, "
+                           "a PDL-chained copy kernel) + kernels.paged_decode_step, then one "
+                           "copy-engine D2H of the output on a copy stream; all steps in one "
+                           "CUDA graph between two event-record nodes",
                     "replay_us_incl_submission": t_e2e_replay * 1e6},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profile_traffic(cfg_name),

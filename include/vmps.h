@@ -139,9 +139,11 @@ int vmps_paged_decode_attention(void* out, const void* q, const void* pool,
  * seq_lens[i] >= 1 and slot_mapping[i] addresses a slot of the last page of
  * sequence i (as the reference's write_info always does for position
  * seq_len-1); otherwise the write is flagged in the error word (bit 32).
- * seq_lens are read before the preceding kernel on the stream finishes
- * (programmatic dependent launch), so they must not be produced by that
- * kernel; q/k/v/positions/slots/tables/pool are read after it finishes.
+ * The launch may start while the kernel before it on the stream still runs
+ * (programmatic dependent launch): the seq_lens and block tables are read
+ * before that kernel finishes, so it must not produce them (pool pages are
+ * only pulled into L2 then, which is coherent with its writes); q/k/v,
+ * positions, slots and the pool contents are read after it finishes.
  * q/k/v rows may have any row stride (slices of a fused QKV output).
  */
 int vmps_paged_decode_step(void* out, void* q, int64_t q_row_stride, const void* k,
@@ -245,6 +247,27 @@ int vmps_silu_mul(void* out, int64_t out_row_stride, const void* gate_up,
 int vmps_decode_gemm_supported(int M, int N, int K, int silu_mul);
 int vmps_decode_gemm(void* out, int64_t out_row_stride, const void* x, int64_t x_row_stride,
                      const void* w, int M, int N, int K, int silu_mul, int dtype, void* stream);
+
+/*
+ * Copies `bytes` from `src` to `dst` with the GPU's own loads and stores,
+ * as a link of a chain of kernels launched with programmatic dependent
+ * launch.  No counterpart in the reference (whose inputs never leave host
+ * memory).  `src` may be pinned host memory: this is how a serving loop
+ * stages a decode step's inputs from the host without a copy-engine copy
+ * between two decode steps, which would cost the second step its early
+ * launch.  The copy starts while the kernel before it on the stream still
+ * runs and does not wait for it; the launch then completes only after that
+ * kernel has, so the kernel after it finds both finished.  Therefore `dst`
+ * must not be read or written by the kernel immediately before this one on
+ * the stream (earlier kernels have completed).  A fused decode step reads
+ * its seq_lens and block tables before its own PDL wait, so between the
+ * stage copy of its inputs and the step itself there must be a kernel that
+ * waits before it lets the next one start (another decode step): stage
+ * step i+1 just before step i (three staging buffers), and stage the first
+ * step of a chain with an ordinary copy.  Both pointers 16-byte aligned,
+ * bytes a multiple of 16.
+ */
+int vmps_stage_copy(void* dst, const void* src, size_t bytes, void* stream);
 
 /*
  * Reads and clears the device error word of the current device (a bitwise OR

@@ -55,6 +55,7 @@ EXPORTED_SYMBOLS = (
     "vmps_silu_mul",
     "vmps_decode_gemm_supported",
     "vmps_decode_gemm",
+    "vmps_stage_copy",
     "vmps_debug_error_word",
 )
 
@@ -107,6 +108,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.vmps_decode_gemm_supported.argtypes = [i32, i32, i32, i32]
         lib.vmps_decode_gemm.restype = i32
         lib.vmps_decode_gemm.argtypes = [vp, i64, vp, i64, vp, i32, i32, i32, i32, i32, vp]
+        lib.vmps_stage_copy.restype = i32
+        lib.vmps_stage_copy.argtypes = [vp, vp, sz, vp]
         lib.vmps_debug_error_word.restype = i32
         lib.vmps_debug_error_word.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
         if path is None:
@@ -522,6 +525,35 @@ def decode_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = Non
                                   int(bool(silu_mul)), dtype_code(x.dtype), _stream(dev))
     _check(rc, "decode_gemm")
     return out
+
+
+def stage_copy(dst: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
+    """Copy ``src`` (pinned host memory or a device tensor) into the CUDA tensor ``dst``
+    with a kernel that is one link of a programmatic-dependent-launch chain.
+
+    It overlaps the kernel before it on the current stream and completes only
+    after that kernel, so ``dst`` must not be in use by that kernel.  A fused
+    decode step reads its lengths and block tables before its own wait: stage
+    step i+1 just before step i (three buffers), the first step with an
+    ordinary copy (``vmps_stage_copy`` in include/vmps.h).  Both tensors
+    contiguous, the same number of bytes (a multiple of 16), 16-byte aligned.
+    """
+    dev = _require_cuda(dst)
+    if src.is_cuda:
+        if src.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {src.device}")
+    elif not src.is_pinned():
+        raise ValueError("stage_copy: a host source must be pinned memory")
+    if not (dst.is_contiguous() and src.is_contiguous()):
+        raise ValueError("stage_copy: tensors must be contiguous")
+    nbytes = dst.numel() * dst.element_size()
+    if src.numel() * src.element_size() != nbytes:
+        raise ValueError("stage_copy: dst and src differ in size")
+    lib = load_library()
+    with torch.cuda.device(dev):
+        rc = lib.vmps_stage_copy(_ptr(dst), _ptr(src), nbytes, _stream(dev))
+    _check(rc, "stage_copy")
+    return dst
 
 
 def error_word(device: torch.device | int | None = None) -> int:
