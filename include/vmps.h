@@ -140,10 +140,11 @@ int vmps_paged_decode_attention(void* out, const void* q, const void* pool,
  * sequence i (as the reference's write_info always does for position
  * seq_len-1); otherwise the write is flagged in the error word (bit 32).
  * The launch may start while the kernel before it on the stream still runs
- * (programmatic dependent launch): the seq_lens and block tables are read
- * before that kernel finishes, so it must not produce them (pool pages are
- * only pulled into L2 then, which is coherent with its writes); q/k/v,
- * positions, slots and the pool contents are read after it finishes.
+ * (programmatic dependent launch): the step metadata -- seq_lens, block
+ * tables, positions, slot_mapping, inv_freq -- is read before that kernel
+ * finishes, so it must not produce them (pool pages are only pulled into L2
+ * then, which is coherent with its writes); q/k/v and the pool contents are
+ * read after it finishes.
  * q/k/v rows may have any row stride (slices of a fused QKV output).
  */
 int vmps_paged_decode_step(void* out, void* q, int64_t q_row_stride, const void* k,
@@ -260,7 +261,7 @@ int vmps_decode_gemm(void* out, int64_t out_row_stride, const void* x, int64_t x
  * kernel has, so the kernel after it finds both finished.  Therefore `dst`
  * must not be read or written by the kernel immediately before this one on
  * the stream (earlier kernels have completed).  A fused decode step reads
- * its seq_lens and block tables before its own PDL wait, so between the
+ * its step metadata before its own PDL wait, so between the
  * stage copy of its inputs and the step itself there must be a kernel that
  * waits before it lets the next one start (another decode step): stage
  * step i+1 just before step i (three staging buffers), and stage the first

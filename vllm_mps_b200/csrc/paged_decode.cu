@@ -103,14 +103,6 @@ constexpr int kPageTokens = 16;
 #define VMPS_DECODE_PREFETCH_BYTES (256 * 1024)
 #endif
 constexpr int kPrefetchBytes = VMPS_DECODE_PREFETCH_BYTES;
-#ifndef VMPS_DECODE_LATE_CTAS
-#define VMPS_DECODE_LATE_CTAS 0
-#endif
-#ifndef VMPS_DECODE_LATE_PCT
-#define VMPS_DECODE_LATE_PCT 100
-#endif
-constexpr long long kLateCtas = VMPS_DECODE_LATE_CTAS;
-constexpr long long kLatePct = VMPS_DECODE_LATE_PCT;
 // 1: a CTA lets the next launch in the stream start before its own PDL wait
 // (the next launch's CTAs then wait for this one to finish, as always).
 #ifndef VMPS_DECODE_EARLY_TRIGGER
@@ -367,16 +359,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
   const int WTP = wpref[num_seqs];
   const long long U = static_cast<long long>(p.num_hg) * TP;
   const long long WU = static_cast<long long>(p.num_hg) * WTP;
-  // The last kLateCtas CTAs of the grid take chunks of kLatePct percent of
-  // the others' weight.  In a chain of launches the CTAs of a launch are
-  // placed on their SMs in index order as the previous launch's CTAs leave,
-  // and the last ones only get the slots of the previous launch's merging
-  // CTAs, which leave last: with full-size chunks they would start streaming
-  // several microseconds after the others and finish last.
-  const long long n_late = kLateCtas < p.n_cta ? kLateCtas : p.n_cta - 1;
-  const long long n_early = p.n_cta - n_late;
-  long long wchunk = (WU * 100 + n_early * 100 + n_late * kLatePct - 1) /
-                     (n_early * 100 + n_late * kLatePct);
+  long long wchunk = (WU + p.n_cta - 1) / p.n_cta;
   // A chunk holds at least kMinPagesPerCta pages.  When sequences average
   // at most 2 * kMinPagesPerCta pages it also holds one sequence start, so
   // short sequences are not cut: a CTA loads a whole one in one or two
@@ -387,16 +370,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
   const bool short_seqs = static_cast<long long>(TP) <= 2LL * kMinPagesPerCta * nonempty;
   const long long kMinChunk = kMinPagesPerCta * kPageWeight + (short_seqs ? kSegmentWeight : 0);
   if (wchunk < kMinChunk) wchunk = kMinChunk;
-  long long wlate = (wchunk * kLatePct + 99) / 100;
-  if (wlate < kMinChunk) wlate = kMinChunk < wchunk ? kMinChunk : wchunk;
-  // Weighted start of CTA b's chunk, and the CTA whose chunk holds w.
-  auto chunk_start = [&](long long b) -> long long {
-    return b <= n_early ? b * wchunk : n_early * wchunk + (b - n_early) * wlate;
-  };
-  auto chunk_of = [&](long long w) -> int {
-    return static_cast<int>(w < n_early * wchunk ? w / wchunk
-                                                 : n_early + (w - n_early * wchunk) / wlate);
-  };
   // First page unit whose weighted position is >= w.
   auto unit_at = [&](long long w) -> long long {
     if (w >= WU) return U;
@@ -413,10 +386,10 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
   auto owner_cta = [&](int hg, int s, int pg) -> int {
     const long long w = static_cast<long long>(hg) * WTP + wpref[s] + kSegmentWeight +
                         static_cast<long long>(pg) * kPageWeight;
-    return chunk_of(w);
+    return static_cast<int>(w / wchunk);
   };
-  const long long u_begin = unit_at(chunk_start(blockIdx.x));
-  const long long u_end = unit_at(chunk_start(blockIdx.x + 1));
+  const long long u_begin = unit_at(static_cast<long long>(blockIdx.x) * wchunk);
+  const long long u_end = unit_at(static_cast<long long>(blockIdx.x + 1) * wchunk);
 
   // Work decode for a unit: its head group and physical block (producer) or
   // its sequence (consumers).
