@@ -127,12 +127,14 @@ def test_c0_greedy_parity_with_reference(c0_model, record_property):
 # Physical mode against the reference's classes run in the same mode
 # (tests/golden/engine_c0_physical.npz: one pool per layer, prompts through
 # the single-token path, 20 greedy steps; make_golden.gen_engine_c0_physical).
-# Measured on a B200 (teacher-forced, all 160 decisions): the logits of the
-# reference's top-5 tokens agree within PHYS_LOGIT_TOL.  The reference's
-# logits are fp16 (one ulp = 0.0039 at magnitude 2-4), and its smallest
-# top-1/top-2 margin is one such ulp; a decision whose margin is below twice
-# the logit tolerance may go either way, every other one must agree.
-PHYS_LOGIT_TOL = 0.05
+# Measured on a B200: all 160 free-running greedy tokens identical, and,
+# teacher-forced, the logits of the reference's top-5 tokens within 0.0098
+# at every decision.  The bars: logits within PHYS_LOGIT_TOL, and the greedy
+# token identical at every decision whose top-1/top-2 margin in the
+# reference exceeds NEAR_TIE (the reference's logits are fp16; its smallest
+# margin in this run is one fp16 ulp, 0.0039, so every decision counts).
+PHYS_LOGIT_TOL = 0.02
+NEAR_TIE = 2e-3
 
 
 def _run_physical_c0(model, forced_tokens=None):
@@ -164,8 +166,8 @@ def _run_physical_c0(model, forced_tokens=None):
 def test_c0_physical_free_running_greedy_parity(c0_model, record_property):
     """Free-running greedy decode in physical mode against the reference run
     in the same mode: every sequence's tokens are identical up to its first
-    divergence, and a divergence may only come at a decision the reference
-    itself calls within 2 * PHYS_LOGIT_TOL (top-1 minus top-2 logit)."""
+    divergence, and a divergence may only come at a near tie (the reference's
+    top-1 minus top-2 logit at most NEAR_TIE)."""
     ours, seen, d = _run_physical_c0(c0_model)
     ref, top_vals = d["tokens"], d["top_vals"]
     margin = top_vals[:, :, 0] - top_vals[:, :, 1]
@@ -175,7 +177,7 @@ def test_c0_physical_free_running_greedy_parity(c0_model, record_property):
         if diff.size:
             t = int(diff[0])
             firsts.append((s, t, float(margin[t, s])))
-            assert margin[t, s] < 2 * PHYS_LOGIT_TOL, (s, t, float(margin[t, s]))
+            assert margin[t, s] <= NEAR_TIE, (s, t, float(margin[t, s]))
     record_property("physical_identical_tokens", int((ours == ref).sum()))
     record_property("physical_identical_sequences", int(sum((ours[s] == ref[s]).all() for s in range(8))))
     record_property("physical_first_divergences", firsts)
@@ -185,7 +187,7 @@ def test_c0_physical_teacher_forced_logits(c0_model, record_property):
     """Teacher-forced with the reference's tokens, all 20 decisions of all 8
     sequences: the logits of the reference's top-5 tokens within
     PHYS_LOGIT_TOL, and the greedy token identical wherever the reference's
-    margin exceeds 2 * PHYS_LOGIT_TOL."""
+    margin exceeds NEAR_TIE."""
     d = load_golden("engine_c0_physical.npz")
     _, seen, d = _run_physical_c0(c0_model, forced_tokens=d["tokens"])
     top_vals, top_ids = d["top_vals"], d["top_ids"]
@@ -200,7 +202,7 @@ def test_c0_physical_teacher_forced_logits(c0_model, record_property):
         for row in range(8):
             if ours_top[row] != top_ids[t, row, 0]:
                 flips.append((t, row, float(margin[row])))
-                assert margin[row] < 2 * PHYS_LOGIT_TOL, (t, row, float(margin[row]))
+                assert margin[row] <= NEAR_TIE, (t, row, float(margin[row]))
     record_property("physical_top5_max_deviation", round(worst, 4))
     record_property("physical_teacher_forced_flips", flips)
     assert worst < PHYS_LOGIT_TOL, worst
