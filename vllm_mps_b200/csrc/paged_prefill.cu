@@ -606,6 +606,32 @@ struct PairShape {
 // first, and within a pair index every (sequence, kv head).  Every role of a
 // CTA walks the same items in the same order (w = blockIdx.x, + gridDim.x,
 // ...), so they agree on every item's tile counts without talking.
+// Pairs (of every 8 in a row of a key tile) whose two exponentials the
+// pair kernel evaluates on the FMA pipe instead of MUFU.
+#ifndef VMPS_PREFILL_EMU_PAIRS
+#define VMPS_PREFILL_EMU_PAIRS 0
+#endif
+constexpr int kEmuPairs = VMPS_PREFILL_EMU_PAIRS;
+
+// 2^x for x <= 0 on the FMA pipe, so the softmax's exponentials are not all
+// queued on the MUFU unit: x = n + f with n = round(x) (the 1.5 * 2^23
+// addition rounds to an integer in the low mantissa bits), f in [-1/2, 1/2];
+// 2^f by a degree-3 polynomial whose coefficients were fitted for this
+// kernel by a Remez exchange on the relative error over [-1/2, 1/2] (max
+// 7.5e-5, 13.7 bits; P is rounded to 8 or 11 bits before the PV MMA); 2^n is
+// added into the exponent field.  x is clamped at -125 (masked keys are -inf
+// and come out as ~2e-38 instead of 0).
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;
+  const float n = t - 12582912.f;
+  const float f = x - n;
+  float q = fmaf(0.0551716685f, f, 0.2426111251f);
+  q = fmaf(q, f, 0.6932609677f);
+  q = fmaf(q, f, 0.9999280572f);
+  return __int_as_float(__float_as_int(q) + ((__float_as_int(t) - 0x4B400000) << 23));
+}
+
 struct PairItem {
   int seq, kvh, tok0, q_len, q_start, row0;
   bool has1;
@@ -663,7 +689,8 @@ __global__ void __launch_bounds__(kPpThreads, 1)
   uint64_t* o_ready = bars + 6;   // [2] MMA -> softmax t: PV_t complete
   uint64_t* o_done = bars + 8;    // [2] MMA -> softmax t: the item's last PV_t complete
   uint64_t* drain = bars + 10;    // MMA lane: everything it issued complete
-  uint64_t* k_full = bars + 11;   // [S]
+  uint64_t* p_half = bars + 11;   // [2] softmax t -> MMA: P_t of the tile's first 64 keys
+  uint64_t* k_full = bars + 13;   // [S]
   uint64_t* k_empty = k_full + S;
   uint64_t* v_full = k_empty + S;
   uint64_t* v_empty = v_full + S;
@@ -687,6 +714,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
       mbar_init(p_full + t, 4);
       mbar_init(o_ready + t, 1);
       mbar_init(o_done + t, 1);
+      mbar_init(p_half + t, 4);
     }
     mbar_init(drain, 1);
     for (int s = 0; s < S; ++s) {
@@ -834,17 +862,26 @@ __global__ void __launch_bounds__(kPpThreads, 1)
           }
           tc_commit(s_full + t);
         };
-        auto pv = [&](int t, int gi, bool first) {  // O_t (+)= P_t V(tile gi)
+        // O_t (+)= P_t V(tile gi) in two halves of 64 keys: the first as soon
+        // as the softmax has written that half of P (p_half), the second
+        // after the rest (p_full).
+        auto pv_half = [&](int t, int gi, bool first, int h) {
           const uint32_t v_addr = smem_u32(sV + (gi % S) * Shape::kTileBytes);
           const uint32_t t_p = tmem_base + Shape::col_s(t);
           const uint32_t t_o = tmem_base + Shape::col_o(t);
 #pragma unroll
-          for (int k = 0; k < KEYS / 16; ++k) {
+          for (int k = h * (KEYS / 32); k < (h + 1) * (KEYS / 32); ++k) {
             const uint64_t b = sw128_desc(v_addr + k * 2048, kPpKRegion, 1024);
             tc_mma_ts(t_o, t_p + k * 8, b, idesc_pv, (!first || k > 0) ? 1u : 0u);
           }
-          tc_commit(o_ready + t);
-          ++pv_cnt[t];
+          if (h == 1) {
+            tc_commit(o_ready + t);
+            ++pv_cnt[t];
+          }
+        };
+        // Waits for P_t of the current tile (half h) and the V tile.
+        auto wait_p = [&](int t, int h) -> bool {
+          return mbar_wait((h ? p_full : p_half) + t, pv_cnt[t] & 1, p.err) && !aborted(abort_flag);
         };
         bool ok = true;
         for (long long w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
@@ -859,21 +896,25 @@ __global__ void __launch_bounds__(kPpThreads, 1)
           for (int j = 0; j < it.n_tiles; ++j) {
             bool v_in = false;
             if (j < it.n_tiles0) {
-              ok = mbar_wait(p_full + 0, pv_cnt[0] & 1, p.err) && !aborted(abort_flag) &&
-                   wait_ring(v_full, g + j);
+              ok = wait_p(0, 0) && wait_ring(v_full, g + j);
               if (!ok) break;
               v_in = true;
-              pv(0, g + j, j == 0);
+              pv_half(0, g + j, j == 0, 0);
+              if (!(ok = wait_p(0, 1))) break;
+              tc_fence_after();
+              pv_half(0, g + j, j == 0, 1);
             }
             const bool next = j + 1 < it.n_tiles;
             if (next && !(ok = wait_ring(k_full, g + j + 1))) break;
             if (j + 1 < it.n_tiles0) qk(0, g + j + 1);
             if (it.has1 && j < it.n_tiles1) {
-              ok = mbar_wait(p_full + 1, pv_cnt[1] & 1, p.err) && !aborted(abort_flag) &&
-                   (v_in || wait_ring(v_full, g + j));
+              ok = wait_p(1, 0) && (v_in || wait_ring(v_full, g + j));
               if (!ok) break;
               tc_fence_after();
-              pv(1, g + j, j == 0);
+              pv_half(1, g + j, j == 0, 0);
+              if (!(ok = wait_p(1, 1))) break;
+              tc_fence_after();
+              pv_half(1, g + j, j == 0, 1);
             }
             tc_commit(v_empty + ((g + j) % S));
             if (it.has1 && j + 1 < it.n_tiles1) qk(1, g + j + 1);
@@ -974,7 +1015,10 @@ __global__ void __launch_bounds__(kPpThreads, 1)
           m_run = m_new;
         }
         // P = exp2(s * scale - m) as 16-bit pairs over the first KEYS/2
-        // columns of this S tile (the A operand of PV in TMEM), 32 keys per store.
+        // columns of this S tile (the A operand of PV in TMEM), 32 keys per
+        // store; the first 64 keys are published (p_half) before the rest
+        // are computed, so the first half of PV runs meanwhile.  kEmuPairs
+        // of every 8 pairs use the FMA-pipe exp2.
         float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c2 = 0; c2 < KEYS / 32; ++c2) {
@@ -983,21 +1027,25 @@ __global__ void __launch_bounds__(kPpThreads, 1)
           for (int h = 0; h < 2; ++h) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              const float a =
-                  fast_exp2(fmaf(__uint_as_float(sr[2 * c2 + h][2 * i]), p.scale_log2, -m_run));
-              const float b = fast_exp2(
-                  fmaf(__uint_as_float(sr[2 * c2 + h][2 * i + 1]), p.scale_log2, -m_run));
+              const float xa = fmaf(__uint_as_float(sr[2 * c2 + h][2 * i]), p.scale_log2, -m_run);
+              const float xb =
+                  fmaf(__uint_as_float(sr[2 * c2 + h][2 * i + 1]), p.scale_log2, -m_run);
+              const bool emu = i >= 8 - kEmuPairs;
+              const float a = emu ? exp2_fma(xa) : fast_exp2(xa);
+              const float b = emu ? exp2_fma(xb) : fast_exp2(xb);
               sum4[i & 3] += a + b;
               pk[h * 8 + i] = Elt<T>::pack(a, b);
             }
           }
           tmem_st16(t_s + c2 * 16, pk);
+          if (c2 == KEYS / 64 - 1 || c2 == KEYS / 32 - 1) {
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive((c2 == KEYS / 32 - 1 ? p_full : p_half) + t);
+          }
         }
-        tmem_st_wait();
         l_run += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(p_full + t);
       }
       if (!ok) break;
       // Epilogue: O / l for the rows of this sequence.  The next item's first
