@@ -42,11 +42,6 @@
 #include "vmps_abi_internal.h"
 #include "vmps_common.cuh"
 
-// 1: the pair kernel (two Q tiles per CTA); 0: one Q tile per CTA, two CTAs per SM.
-#ifndef VMPS_PREFILL_PAIR
-#define VMPS_PREFILL_PAIR 0
-#endif
-
 namespace vmps {
 namespace {
 
@@ -83,7 +78,6 @@ struct PrefillParams {
   int num_seqs, total_q, max_q_len;
   int n_q, n_kv, G, g_shift, num_blocks;
   int tokens_per_tile;  // 128 / G
-  int n_pairs;          // pair kernel: pairs of 128-row tiles in the longest sequence
   float scale_log2;
   int* err;
 };
@@ -556,559 +550,6 @@ int launch_prefill(const CUtensorMap& kv_map, const CUtensorMap& q_map, const Pr
   return check_launch("paged_prefill_attention");
 }
 
-// ── kernel 3, pair form: two 128-row Q tiles per CTA sharing every K/V tile ──
-//
-// One CTA per SM (>= half of its shared memory, all 512 TMEM columns):
-//   TMEM  [0,128) S0 | [128,256) S1 | O0 (D columns) | O1 (D columns)
-//   smem  Q0 | Q1 | K ring (2 x 128 keys) | V ring (2 x 128 keys)
-// The rows of Q tile 1 are the 128 rows after those of Q tile 0 (the next
-// 128/G tokens of the same sequence and kv head), so one K/V load serves 256
-// rows.  Warps 0-3 run the softmax of Q tile 0, warps 4-7 that of Q tile 1
-// (row = TMEM lane), warp 8 loads Q and K, warp 9 loads V, warp 10 (one lane)
-// issues the MMAs (warp 11 idles) in the order
-//   QK0(0) QK1(0) | PV0(j) QK0(j+1) PV1(j) QK1(j+1) | ...
-// so that while one softmax warpgroup works on its S tile the tensor cores
-// run the other tile's PV and next QK.  A key tile is 128 keys (8 pages):
-// with N = 128 a QK MMA reads as many operand bytes per FLOP from shared
-// memory as the SM can deliver, where N = 64 could not.
-constexpr int kPpKeys = 128;
-constexpr int kPpPages = kPpKeys / 16;
-constexpr int kPpStages = 2;
-constexpr int kPpThreads = 384;  // three warpgroups
-constexpr int kPpKWarp = 8;
-constexpr int kPpVWarp = 9;
-constexpr int kPpMmaWarp = 10;      // warp 11 only completes the third warpgroup
-// Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64,512),
-// the load/MMA warpgroup gives up to 96 and the two softmax warpgroups take
-// 200 (256 x 200 + 128 x 96 = 63,488 <= 64,512), so a softmax thread holds
-// its whole 128-key row of S in registers and neither side spills.
-constexpr int kPpRegsSoftmax = 200;
-constexpr int kPpRegsOther = 96;
-constexpr int kPpKRegion = kPpKeys * 128;  // one 64-column chunk of a key tile
-
-template <int D>
-struct PairShape {
-  static constexpr int kChunks = D / 64;
-  static constexpr int kQBytes = kChunks * kRegion;        // one 128-row Q tile
-  static constexpr int kTileBytes = kChunks * kPpKRegion;  // K (or V) of one key tile
-  static constexpr int kBarBytes = 256;
-  static constexpr int kSmemUsed = 2 * kQBytes + 2 * kPpStages * kTileBytes + kBarBytes;
-  // At least half an SM's shared memory: a second CTA placed beside this one
-  // would only wait for the TMEM columns this one holds.
-  static constexpr int kSmemBytes = kSmemUsed > 118 * 1024 ? kSmemUsed : 118 * 1024;
-  static constexpr uint32_t kTmemCols = 512;
-  // TMEM column of S_t and of O_t.
-  static __device__ __forceinline__ uint32_t col_s(int t) { return t ? kPpKeys : 0u; }
-  static __device__ __forceinline__ uint32_t col_o(int t) { return 2u * kPpKeys + (t ? D : 0u); }
-};
-
-// Work item w of the persistent grid: pairs from the last (longest) to the
-// first, and within a pair index every (sequence, kv head).  Every role of a
-// CTA walks the same items in the same order (w = blockIdx.x, + gridDim.x,
-// ...), so they agree on every item's tile counts without talking.
-// Pairs (of every 8 in a row of a key tile) whose two exponentials the
-// pair kernel evaluates on the FMA pipe instead of MUFU.
-#ifndef VMPS_PREFILL_EMU_PAIRS
-#define VMPS_PREFILL_EMU_PAIRS 0
-#endif
-constexpr int kEmuPairs = VMPS_PREFILL_EMU_PAIRS;
-
-// 2^x for x <= 0 on the FMA pipe, so the softmax's exponentials are not all
-// queued on the MUFU unit: x = n + f with n = round(x) (the 1.5 * 2^23
-// addition rounds to an integer in the low mantissa bits), f in [-1/2, 1/2];
-// 2^f by a degree-3 polynomial whose coefficients were fitted for this
-// kernel by a Remez exchange on the relative error over [-1/2, 1/2] (max
-// 7.5e-5, 13.7 bits; P is rounded to 8 or 11 bits before the PV MMA); 2^n is
-// added into the exponent field.  x is clamped at -125 (masked keys are -inf
-// and come out as ~2e-38 instead of 0).
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -125.f);
-  const float t = x + 12582912.f;
-  const float n = t - 12582912.f;
-  const float f = x - n;
-  float q = fmaf(0.0551716685f, f, 0.2426111251f);
-  q = fmaf(q, f, 0.6932609677f);
-  q = fmaf(q, f, 0.9999280572f);
-  return __int_as_float(__float_as_int(q) + ((__float_as_int(t) - 0x4B400000) << 23));
-}
-
-struct PairItem {
-  int seq, kvh, tok0, q_len, q_start, row0;
-  bool has1;
-  int n_tiles0, n_tiles1, n_tiles, n_keys;
-};
-
-__device__ __forceinline__ bool pair_item(const PrefillParams& p, long long w, int keys,
-                                          PairItem& it) {
-  const long long per_pair = static_cast<long long>(p.n_kv) * p.num_seqs;
-  const int pair = p.n_pairs - 1 - static_cast<int>(w / per_pair);
-  const int r = static_cast<int>(w % per_pair);
-  it.seq = r / p.n_kv;
-  it.kvh = r - it.seq * p.n_kv;
-  it.q_len = p.q_lens[it.seq];
-  const int tpt = p.tokens_per_tile;
-  it.tok0 = pair * 2 * tpt;
-  if (it.tok0 >= it.q_len) return false;
-  it.q_start = p.q_start[it.seq];
-  it.row0 = p.cu_q[it.seq];
-  if (it.q_start < 0 || it.row0 < 0 ||
-      static_cast<long long>(it.row0) + it.q_len > p.total_q) {
-    if (threadIdx.x == 0 && it.tok0 == 0 && it.kvh == 0) set_error(p.err, kDevErrQueryRange);
-    return false;
-  }
-  it.has1 = it.tok0 + tpt < it.q_len;
-  const int tok_end0 = min(it.q_len, it.tok0 + tpt);
-  const int tok_end1 = min(it.q_len, it.tok0 + 2 * tpt);
-  it.n_tiles0 = (it.q_start + tok_end0 + keys - 1) / keys;
-  it.n_tiles1 = it.has1 ? (it.q_start + tok_end1 + keys - 1) / keys : 0;
-  it.n_tiles = it.has1 ? it.n_tiles1 : it.n_tiles0;
-  it.n_keys = it.q_start + (it.has1 ? tok_end1 : tok_end0);
-  return true;
-}
-
-template <typename T, int D>
-__global__ void __launch_bounds__(kPpThreads, 1)
-    paged_prefill_pair_kernel(const __grid_constant__ CUtensorMap kv_map,
-                              const __grid_constant__ CUtensorMap q_map, const PrefillParams p) {
-  using Shape = PairShape<D>;
-  constexpr int KEYS = kPpKeys;
-  constexpr int S = kPpStages;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  if (smem_u32(smem_raw) & 1023u) {
-    if (threadIdx.x == 0) set_error(p.err, kDevErrTimeout);
-    return;
-  }
-  uint8_t* sQ = smem_raw;                    // Q0 | Q1
-  uint8_t* sK = sQ + 2 * Shape::kQBytes;     // K ring
-  uint8_t* sV = sK + S * Shape::kTileBytes;  // V ring
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + S * Shape::kTileBytes);
-  uint64_t* q_full = bars + 0;    // loader -> MMA: the item's Q tiles landed
-  uint64_t* q_empty = bars + 1;   // MMA -> loader: the item's last QK read Q
-  uint64_t* s_full = bars + 2;    // [2] MMA -> softmax t: S_t in TMEM
-  uint64_t* p_full = bars + 4;    // [2] softmax t -> MMA: P_t written, O_t rescaled
-  uint64_t* o_ready = bars + 6;   // [2] MMA -> softmax t: PV_t complete
-  uint64_t* o_done = bars + 8;    // [2] MMA -> softmax t: the item's last PV_t complete
-  uint64_t* drain = bars + 10;    // MMA lane: everything it issued complete
-  uint64_t* p_half = bars + 11;   // [2] softmax t -> MMA: P_t of the tile's first 64 keys
-  uint64_t* k_full = bars + 13;   // [S]
-  uint64_t* k_empty = k_full + S;
-  uint64_t* v_full = k_empty + S;
-  uint64_t* v_empty = v_full + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_empty + S);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const long long n_items = static_cast<long long>(p.n_pairs) * p.n_kv * p.num_seqs;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  if (threadIdx.x == 0 && blockIdx.x == 0) {
-    for (int s = 0; s < p.num_seqs; ++s) {
-      if (p.q_lens[s] > p.max_q_len) set_error(p.err, kDevErrQueryRange);
-    }
-  }
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(s_full + t, 1);
-      mbar_init(p_full + t, 4);
-      mbar_init(o_ready + t, 1);
-      mbar_init(o_done + t, 1);
-      mbar_init(p_half + t, 4);
-    }
-    mbar_init(drain, 1);
-    for (int s = 0; s < S; ++s) {
-      mbar_init(k_full + s, 1);
-      mbar_init(k_empty + s, 1);
-      mbar_init(v_full + s, 1);
-      mbar_init(v_empty + s, 1);
-    }
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == kPpMmaWarp) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(Shape::kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  // Each role's code sits inside the branch that sets its register budget
-  // (no path joins the two before the final barrier), so the compiler can
-  // allocate the softmax code with the larger budget.
-  if (warp >= 8) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPpRegsOther));
-    if (warp == kPpKWarp || warp == kPpVWarp) {
-      // ── loads: Q and the K tiles on one warp, the V tiles on another; both
-      // rings run on across items, so the next item's first tiles load while
-      // the current one finishes.  Block ids 32 pages at a time.
-      const bool is_v = warp == kPpVWarp;
-      uint64_t* full = is_v ? v_full : k_full;
-      uint64_t* empty = is_v ? v_empty : k_empty;
-      uint8_t* ring = is_v ? sV : sK;
-      if (lane == 0) {
-        prefetch_tmap(&kv_map);
-        if (!is_v) prefetch_tmap(&q_map);
-      }
-      const int oob = 2 * p.num_blocks;  // past the pool: the TMA fills zeros
-      int g = 0;          // ring tiles issued so far (all items)
-      int items = 0;      // items whose Q was loaded (K warp)
-      bool go = true;
-      for (long long w = blockIdx.x; go && w < n_items; w += gridDim.x) {
-        PairItem it;
-        if (!pair_item(p, w, KEYS, it)) continue;
-        if (!is_v && lane == 0) {
-          if (items > 0 && (!mbar_wait(q_empty, (items - 1) & 1, p.err) || aborted(abort_flag))) {
-            *abort_flag = 1;
-            go = false;
-          } else {
-            mbar_arrive_expect_tx(q_full, (it.has1 ? 2 : 1) * Shape::kQBytes);
-            for (int t = 0; t < (it.has1 ? 2 : 1); ++t) {
-#pragma unroll
-              for (int c = 0; c < Shape::kChunks; ++c) {
-                tma_load_3d(sQ + t * Shape::kQBytes + c * kRegion, &q_map, q_full, c * 64,
-                            it.kvh * p.G, it.row0 + it.tok0 + t * p.tokens_per_tile);
-              }
-            }
-          }
-        }
-        go = __shfl_sync(0xffffffffu, go ? 1 : 0, 0) != 0;
-        if (!go) break;
-        if (!is_v) ++items;
-        const int32_t* table = p.block_tables + static_cast<size_t>(it.seq) * p.max_blocks;
-        const int n_pages = (it.n_keys + 15) >> 4;
-        auto fetch = [&](int page) -> int {  // block id of `page`, or -1
-          if (page >= n_pages) return -1;
-          if (page >= p.max_blocks) {
-            set_error(p.err, kDevErrSeqLen);
-            return -1;
-          }
-          const int b = table[page];
-          if (b < 0 || b >= p.num_blocks) {
-            set_error(p.err, kDevErrBlockRange);
-            return -1;
-          }
-          return b;
-        };
-        int ids = fetch(lane), nxt = fetch(32 + lane), batch = 0;
-        for (int j = 0; j < it.n_tiles; ++j, ++g) {
-          const int page0 = j * kPpPages;
-          if ((page0 >> 5) != batch) {
-            batch = page0 >> 5;
-            ids = nxt;
-            nxt = fetch((batch + 1) * 32 + lane);
-          }
-          int blk[kPpPages];
-#pragma unroll
-          for (int pg = 0; pg < kPpPages; ++pg) {
-            blk[pg] = __shfl_sync(0xffffffffu, ids, (page0 + pg) & 31);
-          }
-          if (lane == 0) {
-            const int st = g % S;
-            if (g >= S &&
-                (!mbar_wait(empty + st, ((g / S) - 1) & 1, p.err) || aborted(abort_flag))) {
-              *abort_flag = 1;
-              go = false;
-            } else {
-              mbar_arrive_expect_tx(full + st, Shape::kTileBytes);
-#pragma unroll
-              for (int pg = 0; pg < kPpPages; ++pg) {
-                const int coord = blk[pg] < 0 ? oob : 2 * blk[pg] + (is_v ? 1 : 0);
-#pragma unroll
-                for (int c = 0; c < Shape::kChunks; ++c) {
-                  tma_load_4d(ring + st * Shape::kTileBytes + c * kPpKRegion + pg * 2048, &kv_map,
-                              full + st, c * 64, 0, it.kvh, coord);
-                }
-              }
-            }
-          }
-          go = __shfl_sync(0xffffffffu, go ? 1 : 0, 0) != 0;
-          if (!go) break;
-        }
-      }
-      if (lane == 0 && aborted(abort_flag)) {
-        // Let this warp's own loads land before the shared memory is released.
-        if (!is_v && items > 0) mbar_wait(q_full, (items - 1) & 1, p.err);
-        for (int j = max(0, g - S); j < g; ++j) mbar_wait(full + (j % S), (j / S) & 1, p.err);
-      }
-    } else if (warp == kPpMmaWarp) {
-      // ── MMA issue (one lane), per item:
-      //   QK0(0) QK1(0) | PV0(j) QK0(j+1) PV1(j) QK1(j+1) | ...
-      if (lane == 0) {
-        const uint32_t idesc_qk = f16_idesc<T>(KEYS, false);
-        const uint32_t idesc_pv = f16_idesc<T>(D, true);
-        int g = 0;             // ring tiles consumed so far (all items)
-        int items = 0;
-        int pv_cnt[2] = {0, 0};
-        auto wait_ring = [&](uint64_t* full, int gi) -> bool {
-          if (!mbar_wait(full + (gi % S), (gi / S) & 1, p.err) || aborted(abort_flag)) return false;
-          tc_fence_after();
-          return true;
-        };
-        auto qk = [&](int t, int gi) {  // S_t = Q_t K(tile gi)^T
-          const uint32_t q_addr = smem_u32(sQ + t * Shape::kQBytes);
-          const uint32_t k_addr = smem_u32(sK + (gi % S) * Shape::kTileBytes);
-          const uint32_t t_s = tmem_base + Shape::col_s(t);
-#pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            const uint64_t a = sw128_desc(q_addr + (k >> 2) * kRegion + (k & 3) * 32, 16, 1024);
-            const uint64_t b =
-                sw128_desc(k_addr + (k >> 2) * kPpKRegion + (k & 3) * 32, 16, 1024);
-            tc_mma(t_s, a, b, idesc_qk, k > 0 ? 1u : 0u);
-          }
-          tc_commit(s_full + t);
-        };
-        // O_t (+)= P_t V(tile gi) in two halves of 64 keys: the first as soon
-        // as the softmax has written that half of P (p_half), the second
-        // after the rest (p_full).
-        auto pv_half = [&](int t, int gi, bool first, int h) {
-          const uint32_t v_addr = smem_u32(sV + (gi % S) * Shape::kTileBytes);
-          const uint32_t t_p = tmem_base + Shape::col_s(t);
-          const uint32_t t_o = tmem_base + Shape::col_o(t);
-#pragma unroll
-          for (int k = h * (KEYS / 32); k < (h + 1) * (KEYS / 32); ++k) {
-            const uint64_t b = sw128_desc(v_addr + k * 2048, kPpKRegion, 1024);
-            tc_mma_ts(t_o, t_p + k * 8, b, idesc_pv, (!first || k > 0) ? 1u : 0u);
-          }
-          if (h == 1) {
-            tc_commit(o_ready + t);
-            ++pv_cnt[t];
-          }
-        };
-        // Waits for P_t of the current tile (half h) and the V tile.
-        auto wait_p = [&](int t, int h) -> bool {
-          return mbar_wait((h ? p_full : p_half) + t, pv_cnt[t] & 1, p.err) && !aborted(abort_flag);
-        };
-        bool ok = true;
-        for (long long w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
-          PairItem it;
-          if (!pair_item(p, w, KEYS, it)) continue;
-          ok = mbar_wait(q_full, items & 1, p.err) && !aborted(abort_flag) && wait_ring(k_full, g);
-          if (!ok) break;
-          qk(0, g);
-          if (it.has1) qk(1, g);
-          tc_commit(k_empty + (g % S));
-          if (it.n_tiles == 1) tc_commit(q_empty);
-          for (int j = 0; j < it.n_tiles; ++j) {
-            bool v_in = false;
-            if (j < it.n_tiles0) {
-              ok = wait_p(0, 0) && wait_ring(v_full, g + j);
-              if (!ok) break;
-              v_in = true;
-              pv_half(0, g + j, j == 0, 0);
-              if (!(ok = wait_p(0, 1))) break;
-              tc_fence_after();
-              pv_half(0, g + j, j == 0, 1);
-            }
-            const bool next = j + 1 < it.n_tiles;
-            if (next && !(ok = wait_ring(k_full, g + j + 1))) break;
-            if (j + 1 < it.n_tiles0) qk(0, g + j + 1);
-            if (it.has1 && j < it.n_tiles1) {
-              ok = wait_p(1, 0) && (v_in || wait_ring(v_full, g + j));
-              if (!ok) break;
-              tc_fence_after();
-              pv_half(1, g + j, j == 0, 0);
-              if (!(ok = wait_p(1, 1))) break;
-              tc_fence_after();
-              pv_half(1, g + j, j == 0, 1);
-            }
-            tc_commit(v_empty + ((g + j) % S));
-            if (it.has1 && j + 1 < it.n_tiles1) qk(1, g + j + 1);
-            if (next) tc_commit(k_empty + ((g + j + 1) % S));
-            if (j + 2 == it.n_tiles) tc_commit(q_empty);  // every QK of the item issued
-          }
-          if (!ok) break;
-          tc_commit(o_done + 0);
-          if (it.has1) tc_commit(o_done + 1);
-          g += it.n_tiles;
-          ++items;
-        }
-        if (!ok) *abort_flag = 1;
-        // Whatever happened, every MMA this lane issued completes before the
-        // TMEM is freed.
-        tc_commit(drain);
-        mbar_wait(drain, 0, p.err);
-      }
-    }
-  } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPpRegsSoftmax));
-    // ── softmax and epilogue of Q tile t: one row per thread ─────────────────
-    const int t = warp >> 2;
-    const int m = threadIdx.x & 127;  // row = TMEM lane
-    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t t_s = tmem_base + lane_base + Shape::col_s(t);
-    const uint32_t t_o = tmem_base + lane_base + Shape::col_o(t);
-    const int tk = m >> p.g_shift;
-    int tiles_done = 0;  // S_t tiles processed (all items): s_full / o_ready phases
-    int items = 0;       // items with a tile t processed: o_done[t] phase
-    bool ok = true;
-    for (long long w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
-      PairItem it;
-      if (!pair_item(p, w, KEYS, it)) continue;
-      if (t == 1 && !it.has1) continue;
-      const int my_tiles = t ? it.n_tiles1 : it.n_tiles0;
-      const int tok_base = it.tok0 + t * p.tokens_per_tile;
-      const int row_pos = it.q_start + tok_base + tk;
-      float m_run = -INFINITY;
-      float l_run = 0.f;
-      for (int j = 0; j < my_tiles; ++j, ++tiles_done) {
-        ok = mbar_wait(s_full + t, tiles_done & 1, p.err);
-        ok = __all_sync(0xffffffffu, ok) && !aborted(abort_flag);
-        if (!ok) break;
-        tc_fence_after();
-        uint32_t sr[KEYS / 16][16];
-#pragma unroll
-        for (int c = 0; c < KEYS / 16; ++c) tmem_ld16(t_s + c * 16, sr[c]);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < KEYS / 16; ++c) tmem_ld_fence_regs(sr[c]);
-        const int key0 = j * KEYS;
-        // Max on raw scores (the scale is positive), the scale folded into
-        // the exp2 argument; keys past the row's position are -inf.  The
-        // warp takes the masked path together when any of its rows needs it.
-        const bool needs_mask = __any_sync(0xffffffffu, key0 + KEYS - 1 > row_pos);
-        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (needs_mask) {
-#pragma unroll
-          for (int c = 0; c < KEYS / 16; ++c) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              if (key0 + c * 16 + i > row_pos) sr[c][i] = __float_as_uint(-INFINITY);
-              mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(sr[c][i]));
-            }
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < KEYS / 16; ++c) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(sr[c][i]));
-          }
-        }
-        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
-        const float m_new = fmaxf(m_run, mx);
-        if (j == 0) {
-          m_run = m_new;
-        } else if (__any_sync(0xffffffffu, m_new > m_run + 8.f)) {
-          // Rescale this warp's O rows once PV_t of the previous tile has
-          // landed (only it can have completed since: the next PV_t waits for
-          // this tile's P).
-          ok = mbar_wait(o_ready + t, (tiles_done - 1) & 1, p.err);
-          ok = __all_sync(0xffffffffu, ok) && !aborted(abort_flag);
-          if (!ok) break;
-          tc_fence_after();
-          const float alpha = fast_exp2(m_run - m_new);
-#pragma unroll
-          for (int c = 0; c < D / 16; ++c) {
-            uint32_t o[16];
-            tmem_ld16(t_o + c * 16, o);
-            tmem_ld_wait();
-            tmem_ld_fence_regs(o);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st16(t_o + c * 16, o);
-          }
-          l_run *= alpha;
-          m_run = m_new;
-        }
-        // P = exp2(s * scale - m) as 16-bit pairs over the first KEYS/2
-        // columns of this S tile (the A operand of PV in TMEM), 32 keys per
-        // store; the first 64 keys are published (p_half) before the rest
-        // are computed, so the first half of PV runs meanwhile.  kEmuPairs
-        // of every 8 pairs use the FMA-pipe exp2.
-        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int c2 = 0; c2 < KEYS / 32; ++c2) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float xa = fmaf(__uint_as_float(sr[2 * c2 + h][2 * i]), p.scale_log2, -m_run);
-              const float xb =
-                  fmaf(__uint_as_float(sr[2 * c2 + h][2 * i + 1]), p.scale_log2, -m_run);
-              const bool emu = i >= 8 - kEmuPairs;
-              const float a = emu ? exp2_fma(xa) : fast_exp2(xa);
-              const float b = emu ? exp2_fma(xb) : fast_exp2(xb);
-              sum4[i & 3] += a + b;
-              pk[h * 8 + i] = Elt<T>::pack(a, b);
-            }
-          }
-          tmem_st16(t_s + c2 * 16, pk);
-          if (c2 == KEYS / 64 - 1 || c2 == KEYS / 32 - 1) {
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive((c2 == KEYS / 32 - 1 ? p_full : p_half) + t);
-          }
-        }
-        l_run += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-      }
-      if (!ok) break;
-      // Epilogue: O / l for the rows of this sequence.  The next item's first
-      // PV_t waits for this thread's next P, so O_t stays until it is read.
-      ok = mbar_wait(o_done + t, items & 1, p.err);
-      ok = __all_sync(0xffffffffu, ok) && !aborted(abort_flag);
-      ++items;
-      if (!ok) break;
-      tc_fence_after();
-      const float inv_l = 1.f / l_run;
-      const bool valid = tok_base + tk < it.q_len;
-      T* orow = static_cast<T*>(p.out) +
-                (static_cast<size_t>(it.row0 + tok_base + tk) * p.n_q + it.kvh * p.G +
-                 (m & (p.G - 1))) * D;
-#pragma unroll
-      for (int c = 0; c < D / 16; ++c) {
-        uint32_t o[16];
-        tmem_ld16(t_o + c * 16, o);
-        tmem_ld_wait();
-        tmem_ld_fence_regs(o);
-        uint32_t packed[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          packed[i] = Elt<T>::pack(__uint_as_float(o[2 * i]) * inv_l,
-                                   __uint_as_float(o[2 * i + 1]) * inv_l);
-        }
-        if (valid) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 16);
-          dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-          dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-        }
-      }
-      tc_fence_before();  // the TMEM reads of O_t come before the next item's PV_t
-    }
-    if (!ok) *abort_flag = 1;
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == kPpMmaWarp) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(Shape::kTmemCols)
-                 : "memory");
-  }
-}
-
-template <typename T, int D>
-int launch_prefill_pair(const CUtensorMap& kv_map, const CUtensorMap& q_map,
-                        const PrefillParams& p, dim3 grid, cudaStream_t s) {
-  using Shape = PairShape<D>;
-  static std::once_flag flags[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return fail(VMPS_ERR_CUDA, "device index %d", dev);
-  std::call_once(flags[dev], [] {
-    cudaFuncSetAttribute(paged_prefill_pair_kernel<T, D>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmemBytes);
-  });
-  paged_prefill_pair_kernel<T, D><<<grid, kPpThreads, Shape::kSmemBytes, s>>>(kv_map, q_map, p);
-  return check_launch("paged_prefill_attention");
-}
-
 }  // namespace
 }  // namespace vmps
 
@@ -1211,24 +652,9 @@ extern "C" int vmps_paged_prefill_attention(
   p.tokens_per_tile = tpt;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-#if VMPS_PREFILL_PAIR
-  {
-    // Persistent: one CTA per SM walks the work items.
-    p.n_pairs = (max_q_len + 2 * tpt - 1) / (2 * tpt);
-    int sms = 0;
-    if (int rc = device_sm_count(&sms)) return rc;
-    const long long n_items = static_cast<long long>(p.n_pairs) * n_kv * num_seqs;
-    const dim3 grid(static_cast<unsigned>(n_items < sms ? n_items : sms));
-    if (dtype == VMPS_DTYPE_F16) {
-      return head_dim == 64 ? launch_prefill_pair<__half, 64>(kv_map, q_map, p, grid, s)
-                            : launch_prefill_pair<__half, 128>(kv_map, q_map, p, grid, s);
-    }
-    return head_dim == 64 ? launch_prefill_pair<__nv_bfloat16, 64>(kv_map, q_map, p, grid, s)
-                          : launch_prefill_pair<__nv_bfloat16, 128>(kv_map, q_map, p, grid, s);
-  }
-#endif
   const dim3 grid((max_q_len + tpt - 1) / tpt, n_kv, num_seqs);
+  if (grid.x > 0x7fffffffu) return fail(VMPS_ERR_UNSUPPORTED, "%s: grid too large", what);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == VMPS_DTYPE_F16) {
     return head_dim == 64 ? launch_prefill<__half, 64>(kv_map, q_map, p, grid, s)
                           : launch_prefill<__half, 128>(kv_map, q_map, p, grid, s);
