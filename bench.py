@@ -857,7 +857,7 @@ def run_engine(args, rank, world, local_rank):
     blocks = int(sum((int(n) + steps + 16) // 16 + 1 for n in lens)) + 16
     eng = LLMEngine.from_model(model, num_gpu_blocks=blocks, num_cpu_blocks=16, max_batch_size=B,
                                max_tokens_per_step=10 ** 9, mode="physical", dtype=dt, device=dev,
-                               max_prefill_rows=16384)
+                               max_prefill_rows=16384, pipeline=not args.sync_engine)
     eng.capture_decode_graphs()  # startup work, outside the timed region
     for p in prompts:
         eng.add_request(p, SamplingParams(temperature=0.0, max_tokens=steps + 1))
@@ -909,11 +909,13 @@ def run_engine(args, rank, world, local_rank):
                        "seq_len": f"prompts U[{plo},{phi}] + {steps} generated",
                        "parallelism": f"sequence-sharded x{world}",
                        "prefill_s_first_step": t_prefill,
+                       "engine_loop": "synchronous" if args.sync_engine else "pipelined",
                        "timing": "CUDA events around the engine's step() calls"},
             "e2e": {"value": toks / t, "unit": "tokens/s",
                     "h2d_bytes_per_step": B * 8 + B * (int(ctx_mean) // 16 + 4) * 4,
                     "d2h_bytes_per_step": B * 8,
-                    "api": "LLMEngine.step(): host token ids in, host token ids out"},
+                    "api": "LLMEngine.step(): host token ids in, host token ids out "
+                           "(pipelined: each call returns the previous launch's ids)"},
             "roofline": {"bound": "hbm", "achieved": step_bytes / t_step / 1e9, "peak": peak,
                          "unit": "GB/s", "frac": step_bytes / t_step / 1e9 / peak,
                          "traffic": None, "peak_kind": peak_kind,
@@ -977,7 +979,7 @@ def c4_leg(args, rank, world, local_rank, n_req=1024):
     eng = LLMEngine.from_model(model, num_gpu_blocks=16384, num_cpu_blocks=4096,
                                max_batch_size=256, max_tokens_per_step=10 ** 9, mode="physical",
                                preempt_watermark=0.9, dtype=torch.float16, device=dev,
-                               max_prefill_rows=16384)
+                               max_prefill_rows=16384, pipeline=not args.sync_engine)
     dist = None
     if world > 1:
         import torch.distributed as dist
@@ -1038,6 +1040,7 @@ def c4_leg(args, rank, world, local_rank, n_req=1024):
         "data": "synthetic (random-init weights, seeded lognormal prompts)",
         "config": {"workload": C4 if n_req == 1024 else f"{C4} [first {n_req} requests]",
                    "global_batch": n_req, "parallelism": f"sequence-sharded x{world}",
+                   "engine_loop": "synchronous" if args.sync_engine else "pipelined",
                    "prompt_tokens": int(p_lens.sum()), "generated_tokens": int(o_lens.sum()),
                    "timing": "CUDA events around the whole run, max over ranks"},
         "per_rank": {"run_s": per_rank[:, 0].round(4).tolist(),
@@ -1281,6 +1284,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-subrecords", action="store_true",
                     help="c1: skip the c3 / prefill / sharded-engine sub-records")
+    ap.add_argument("--sync-engine", action="store_true",
+                    help="engine configs: the synchronous step loop instead of the pipelined one")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -223,12 +223,25 @@ int vmps_paged_prefill_attention(void* out, const void* q, int64_t q_row_stride,
  *   out <- weight * (residual * rsqrt(mean(residual^2) + eps)) for `rows`
  *   rows of `hidden` elements (hidden % 8 == 0; rows 16-byte aligned).
  * vmps_silu_mul: out[:, :inter] <- silu(gate_up[:, :inter]) * gate_up[:, inter:2*inter].
+ * vmps_embed_rmsnorm: the step's first kernel (the HF embedding lookup and
+ *   the first layer's input LlamaRMSNorm).  Row i's token is prev[src[i]]
+ *   when src is non-NULL and src[i] >= 0 (an id the previous step sampled on
+ *   the device: a pipelined engine launches step k+1 before it reads step
+ *   k's tokens back), else tokens[i]; residual[i] <- table[token] (table:
+ *   [vocab, hidden]), out[i] <- RMSNorm(residual[i]) * weight as
+ *   vmps_add_rmsnorm with delta NULL.  src[i] >= n_prev or a token outside
+ *   [0, vocab) sets error bit 128 and zeroes the row.
  */
 int vmps_add_rmsnorm(void* out, int64_t out_row_stride, void* residual, int64_t res_row_stride,
                      const void* delta, int64_t delta_row_stride, const void* weight, int rows,
                      int hidden, float eps, int dtype, void* stream);
 int vmps_silu_mul(void* out, int64_t out_row_stride, const void* gate_up,
                   int64_t in_row_stride, int rows, int inter, int dtype, void* stream);
+int vmps_embed_rmsnorm(void* out, int64_t out_row_stride, void* residual,
+                       int64_t res_row_stride, const void* table, int64_t vocab,
+                       const int32_t* tokens, const int32_t* src, const int64_t* prev,
+                       int n_prev, const void* weight, int rows, int hidden, float eps,
+                       int dtype, void* stream);
 
 /*
  * Decode GEMM for the projections around the attention step at decode batch

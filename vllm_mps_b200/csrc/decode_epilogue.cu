@@ -14,8 +14,11 @@
 //    reduction of the fp32 sum of squares.
 //  * silu_mul: out <- round(round(silu(gate)) * up) for a fused [gate | up]
 //    GEMM output row, silu(g) = g / (1 + exp(-g)) in fp32.
+//  * embed_rmsnorm: the step's token ids (from the host, or from the previous
+//    step's device-side sampling), their embedding rows and the first
+//    layer's input RMSNorm in one kernel.
 //
-// Both are HBM-bound at any size (a few FLOPs per byte).
+// All are HBM-bound at any size (a few FLOPs per byte).
 #include <type_traits>
 
 #include "vmps_abi_internal.h"
@@ -26,8 +29,8 @@ namespace {
 
 constexpr int kNormThreads = 256;
 
-// Both kernels are launched with programmatic dependent launch: they wait for
-// the previous kernel's outputs, then at once let the next kernel launch (a
+// Every kernel here is launched with programmatic dependent launch: it waits for
+// the previous kernel's outputs, then at once lets the next kernel launch (a
 // decode GEMM then streams its weights while this kernel runs).
 __device__ __forceinline__ void pdl_enter() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -103,6 +106,70 @@ __global__ void __launch_bounds__(kNormThreads)
   }
 }
 
+// First kernel of a decode step: each row's input token, its embedding row
+// (the residual stream) and the first layer's input RMSNorm.  The token of
+// row i is prev[src[i]] when src is given and src[i] >= 0 (the id the
+// previous step sampled on the device, so the host need not wait for it),
+// else tokens[i].  residual <- table[token] (an exact copy, as an embedding
+// lookup); out <- RMSNorm(residual) * weight with add_rmsnorm's rounding
+// points.  A src entry at or above n_prev, or a token outside [0, vocab),
+// sets kDevErrTokenRange and the row becomes zeros.
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads)
+    embed_rmsnorm_kernel(T* __restrict__ out, T* __restrict__ residual,
+                         const T* __restrict__ table, int64_t vocab,
+                         const int32_t* __restrict__ tokens, const int32_t* __restrict__ src,
+                         const int64_t* __restrict__ prev, int n_prev, const T* __restrict__ weight,
+                         int hidden, int64_t out_stride, int64_t res_stride, float eps, int* err) {
+  pdl_enter();
+  const int row = blockIdx.x;
+  int64_t tok = tokens[row];
+  if (src) {
+    const int s = src[row];
+    if (s >= 0) tok = s < n_prev ? prev[s] : int64_t(-1);
+  }
+  const bool ok = tok >= 0 && tok < vocab;
+  if (!ok && threadIdx.x == 0) set_error(err, kDevErrTokenRange);
+  const uint4* e = reinterpret_cast<const uint4*>(table + (ok ? tok : 0) * hidden);
+  T* r = residual + row * res_stride;
+  T* o = out + row * out_stride;
+  const int n8 = hidden / 8;
+  float ss = 0.f;
+  for (int v = threadIdx.x; v < n8; v += kNormThreads) {
+    uint4 rv = ok ? e[v] : make_uint4(0u, 0u, 0u, 0u);
+    reinterpret_cast<uint4*>(r)[v] = rv;
+    const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float x = Elt<T>::to_f(re[k]);
+      ss = fmaf(x, x, ss);
+    }
+  }
+  __shared__ float part[kNormThreads / 32];
+#pragma unroll
+  for (int sh = 16; sh > 0; sh >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, sh);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) tot += part[w];
+  const float inv = rsqrtf(tot / static_cast<float>(hidden) + eps);
+  for (int v = threadIdx.x; v < n8; v += kNormThreads) {
+    const uint4 rv = reinterpret_cast<const uint4*>(r)[v];
+    const uint4 wv = reinterpret_cast<const uint4*>(weight)[v];
+    const T* re = reinterpret_cast<const T*>(&rv);
+    const T* we = reinterpret_cast<const T*>(&wv);
+    uint4 ov;
+    T* oe = reinterpret_cast<T*>(&ov);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const T xn = Elt<T>::from_f(Elt<T>::to_f(re[k]) * inv);
+      oe[k] = Elt<T>::from_f(Elt<T>::to_f(we[k]) * Elt<T>::to_f(xn));
+    }
+    reinterpret_cast<uint4*>(o)[v] = ov;
+  }
+}
+
 template <typename T>
 __global__ void silu_mul_kernel(T* __restrict__ out, const T* __restrict__ gate_up, int inter,
                                 int64_t out_stride, int64_t in_stride) {
@@ -169,6 +236,50 @@ extern "C" int vmps_add_rmsnorm(void* out, int64_t out_stride, void* residual, i
   }
   if (e != cudaSuccess) {
     return fail(VMPS_ERR_CUDA, "add_rmsnorm: launch failed: %s", cudaGetErrorString(e));
+  }
+  return VMPS_OK;
+}
+
+extern "C" int vmps_embed_rmsnorm(void* out, int64_t out_stride, void* residual,
+                                  int64_t res_stride, const void* table, int64_t vocab,
+                                  const int32_t* tokens, const int32_t* src, const int64_t* prev,
+                                  int n_prev, const void* weight, int rows, int hidden, float eps,
+                                  int dtype, void* stream) {
+  clear_error();
+  if (rows < 0 || hidden <= 0 || hidden % 8 || vocab <= 0 || !(eps >= 0.f)) {
+    return fail(VMPS_ERR_INVALID_ARG, "embed_rmsnorm: rows=%d hidden=%d vocab=%lld eps=%g", rows,
+                hidden, (long long)vocab, (double)eps);
+  }
+  if (rows == 0) return VMPS_OK;
+  if (!out || !residual || !table || !tokens || !weight || (src && (!prev || n_prev < 0))) {
+    return fail(VMPS_ERR_INVALID_ARG, "embed_rmsnorm: NULL pointer or n_prev < 0");
+  }
+  if (!aligned_rows(out, out_stride) || !aligned_rows(residual, res_stride) || !aligned16(table) ||
+      !aligned16(weight)) {
+    return fail(VMPS_ERR_ALIGNMENT,
+                "embed_rmsnorm: rows must be 16-byte aligned with strides multiples of 8 elements");
+  }
+  if (dtype != VMPS_DTYPE_F16 && dtype != VMPS_DTYPE_BF16) {
+    return fail(VMPS_ERR_INVALID_ARG, "embed_rmsnorm: dtype %d", dtype);
+  }
+  int* err = nullptr;
+  if (int rc = device_error_word(&err)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (dtype == VMPS_DTYPE_F16) {
+    e = launch_pdl(embed_rmsnorm_kernel<__half>, dim3(rows), dim3(kNormThreads), s,
+                   static_cast<__half*>(out), static_cast<__half*>(residual),
+                   static_cast<const __half*>(table), vocab, tokens, src, prev, n_prev,
+                   static_cast<const __half*>(weight), hidden, out_stride, res_stride, eps, err);
+  } else {
+    e = launch_pdl(embed_rmsnorm_kernel<__nv_bfloat16>, dim3(rows), dim3(kNormThreads), s,
+                   static_cast<__nv_bfloat16*>(out), static_cast<__nv_bfloat16*>(residual),
+                   static_cast<const __nv_bfloat16*>(table), vocab, tokens, src, prev, n_prev,
+                   static_cast<const __nv_bfloat16*>(weight), hidden, out_stride, res_stride, eps,
+                   err);
+  }
+  if (e != cudaSuccess) {
+    return fail(VMPS_ERR_CUDA, "embed_rmsnorm: launch failed: %s", cudaGetErrorString(e));
   }
   return VMPS_OK;
 }

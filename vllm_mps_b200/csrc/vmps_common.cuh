@@ -26,6 +26,7 @@ enum DevErr : int {
   kDevErrPositionRange = 16, // negative position
   kDevErrSlotNotLast = 32,   // fused step: new-token slot not in the sequence's last page
   kDevErrQueryRange = 64,    // prefill: q rows outside [0, total_q) or q_len > max_q_len
+  kDevErrTokenRange = 128,   // embed_rmsnorm: token id outside [0, vocab)
 };
 
 __device__ __forceinline__ void set_error(int* err, int bit) {

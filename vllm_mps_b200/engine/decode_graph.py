@@ -23,12 +23,18 @@ their rounding points, minus the model-level work a decode step does not use
 (masks and rotary tables: RoPE runs inside the decode kernel).  Other models
 replay the HF submodules in the same order.
 
-Per step the host packs block tables, lengths, positions, slots and token ids
-of the batch, padded to the bucket (padding rows have length 0 and no slot:
-the kernel writes zeros for them and touches no slot), into one pinned
-buffer; one H2D copy moves it into the bucket's static device buffer and the
-graph is replayed.  Block tables are ``max_blocks`` wide; a step whose
-tables are wider, or a batch above the largest bucket, runs eagerly.
+Per step the host packs block tables, lengths, positions, slots, token ids
+and token sources of the batch, padded to the bucket (padding rows have
+length 0 and no slot: the kernel writes zeros for them and touches no slot),
+into one of the bucket's two pinned buffers (alternating, so packing step
+k+1 never overwrites a buffer whose copy for step k may still be queued);
+one H2D copy moves it into the bucket's static device buffer and the graph
+is replayed.  The graph's first kernel (``kernels.embed_rmsnorm``) takes row
+i's token from the host ids, or -- when its source entry is >= 0 -- from
+``prev_tokens``, the device buffer the previous step's sampler wrote: that
+is what lets a pipelined engine launch a step before it has read the last
+one's tokens back.  Block tables are ``max_blocks`` wide; a step whose tables
+are wider, or a batch above the largest bucket, runs eagerly.
 """
 
 from __future__ import annotations
@@ -60,6 +66,9 @@ class DecodeGraphRunner:
         self._graphs: dict[int, tuple] = {}
         self._pool = None
         self._gate_up = self._fuse_gate_up() if self._llama_layers() else None
+        # Sampled ids of the last step, one per batch row (written by the
+        # engine's sampler, read by the next replay through the source row).
+        self.prev_tokens = torch.zeros(BUCKETS[-1], dtype=torch.long, device=self.device)
 
     def _llama_layers(self) -> bool:
         """Whether every layer is RMSNorm + bias-free SiLU-gated MLP (the fused path)."""
@@ -82,6 +91,9 @@ class DecodeGraphRunner:
                 return False
             if mlp.gate_proj.out_features % 8 or hid % 8:
                 return False
+        # The embedding lookup is fused into the first kernel: a plain table.
+        if type(m.embed_tokens) is not nn.Embedding or m.embed_tokens.max_norm is not None:
+            return False
         return hasattr(m.norm, "variance_epsilon")
 
     def _fuse_gate_up(self) -> list[torch.Tensor]:
@@ -114,7 +126,8 @@ class DecodeGraphRunner:
         Bb = self.bucket(batch) or batch
         d = self.adapter.model_config.d_model
         a0 = m.model.layers[0].self_attn
-        n = nl + 2 * nl + 1  # decode step; residual + RMSNorm twice a layer, plus the first
+        # decode step; residual + RMSNorm twice a layer; embedding + the first RMSNorm
+        n = nl + 2 * nl + 1
         n += nl * (K.decode_gemm_supported(Bb, a0._w_qkv.shape[0], d)
                    + K.decode_gemm_supported(Bb, d, a0.W_O.in_features))
         n += nl  # the [gate|up] decode GEMM with SiLU * up, or silu_mul after cuBLAS
@@ -137,6 +150,7 @@ class DecodeGraphRunner:
             return self._forward_fused(st)
         m = self.adapter.hf_model
         meta = st.meta
+        # Device-sourced tokens are a fused-path feature: ``run`` refuses them here.
         x = m.model.embed_tokens(st.tokens).unsqueeze(1)
         for layer in m.model.layers:
             r = x
@@ -149,20 +163,22 @@ class DecodeGraphRunner:
         st.logits.copy_(m.lm_head(x[:, 0, :]))
 
     def _forward_fused(self, st) -> None:
-        """Per layer: QKV GEMM, decode-step kernel, O GEMM, add+RMSNorm,
-        [gate|up] GEMM, SiLU*up, down GEMM, add+RMSNorm (the next layer's input
-        norm, or the final norm) -- 8 kernels."""
+        """Tokens, embedding and the first RMSNorm in one kernel; then per
+        layer: QKV GEMM, decode-step kernel, O GEMM, add+RMSNorm, [gate|up]
+        GEMM, SiLU*up, down GEMM, add+RMSNorm (the next layer's input norm, or
+        the final norm) -- 8 kernels."""
         from vllm_mps_b200 import kernels as K
         from vllm_mps_b200.layers.paged_attention_layer import PagedAttentionLayer
 
         project = PagedAttentionLayer.project
         m = self.adapter.hf_model
         layers = m.model.layers
-        res = m.model.embed_tokens(st.tokens)  # (Bb, d): the residual stream
-        h = torch.empty_like(res)
-        Bb, d = res.shape
         first = layers[0].input_layernorm
-        K.add_rmsnorm(res, first.weight, first.variance_epsilon, out=h)
+        # res (Bb, d): the residual stream; h: its normalised copy.
+        res, h = K.embed_rmsnorm(m.model.embed_tokens.weight, first.weight,
+                                 first.variance_epsilon, st.tokens, src=st.src,
+                                 prev=self.prev_tokens)
+        Bb, d = res.shape
         for i, layer in enumerate(layers):
             attn = layer.self_attn._attend(h.unsqueeze(1), st.meta)
             post = layer.post_attention_layernorm
@@ -183,11 +199,13 @@ class DecodeGraphRunner:
             st.logits.copy_(head(h))
 
     def _static(self, Bb: int):
-        """Static buffers of a bucket: [tables Bb x W | lengths | positions | slots | tokens]."""
+        """Static buffers of a bucket:
+        [tables Bb x W | lengths | positions | slots | tokens | token sources]."""
         W = self.max_blocks
-        n = Bb * W + 4 * Bb
+        n = Bb * W + 5 * Bb
         dev = torch.zeros(n, dtype=torch.int32, device=self.device)
-        host = torch.zeros(n, dtype=torch.int32).pin_memory()
+        hosts = [torch.zeros(n, dtype=torch.int32).pin_memory() for _ in range(2)]
+        copied = [torch.cuda.Event() for _ in range(2)]
         o = Bb * W
         meta = SimpleNamespace(bt_tensor=dev[:o].view(Bb, W), sl_tensor=dev[o:o + Bb],
                                pos_tensor=dev[o + Bb:o + 2 * Bb],
@@ -195,13 +213,18 @@ class DecodeGraphRunner:
         vocab = self.adapter.hf_model.lm_head.out_features
         logits = torch.empty((Bb, vocab), dtype=self.adapter.model_config.dtype,
                              device=self.device)
-        return SimpleNamespace(Bb=Bb, W=W, dev=dev, host=host, meta=meta,
-                               tokens=dev[o + 3 * Bb:], logits=logits)
+        return SimpleNamespace(Bb=Bb, W=W, dev=dev, hosts=hosts, copied=copied, turn=0,
+                               meta=meta, tokens=dev[o + 3 * Bb:o + 4 * Bb],
+                               src=dev[o + 4 * Bb:], logits=logits)
 
-    def _stage(self, st, token_ids, seq_ids, positions, seq_lens) -> None:
+    def _stage(self, st, token_ids, seq_ids, positions, seq_lens, src=None) -> None:
         """Pack the batch (padded to the bucket) into pinned memory; one H2D copy."""
         B, Bb, W = len(seq_ids), st.Bb, st.W
-        h = st.host.numpy()
+        j = st.turn
+        st.turn ^= 1
+        st.copied[j].synchronize()  # this buffer's previous copy has left it
+        host = st.hosts[j]
+        h = host.numpy()
         h[:] = 0
         bt = h[:Bb * W].reshape(Bb, W)
         for i, sid in enumerate(seq_ids):
@@ -215,7 +238,11 @@ class DecodeGraphRunner:
         h[o + 2 * Bb:o + 3 * Bb] = -1  # padding rows own no slot
         h[o + 2 * Bb:o + 2 * Bb + B] = blk * self.block_size + pos % self.block_size
         h[o + 3 * Bb:o + 3 * Bb + B] = token_ids
-        st.dev.copy_(st.host, non_blocking=True)
+        h[o + 4 * Bb:] = -1  # host token ids unless a source row is given
+        if src is not None:
+            h[o + 4 * Bb:o + 4 * Bb + B] = src
+        st.dev.copy_(host, non_blocking=True)
+        st.copied[j].record()
 
     def _capture(self, Bb: int):
         st = self._static(Bb)
@@ -243,14 +270,21 @@ class DecodeGraphRunner:
             return False
         return all(len(self.kv.get_block_ids(s)) <= self.max_blocks for s in seq_ids)
 
-    def run(self, token_ids, seq_ids, positions, seq_lens) -> torch.Tensor:
-        """Logits ``(B, vocab)`` of one decode step (a view of the bucket's static buffer)."""
+    def run(self, token_ids, seq_ids, positions, seq_lens, src=None) -> torch.Tensor:
+        """Logits ``(B, vocab)`` of one decode step (a view of the bucket's static buffer).
+
+        ``src`` (optional, one int per row): ``src[i] >= 0`` takes row i's
+        token from ``prev_tokens[src[i]]`` on the device instead of
+        ``token_ids[i]`` (fused Llama path only).
+        """
+        if src is not None and self._gate_up is None:
+            raise ValueError("device-sourced tokens need the fused Llama decode step")
         B = len(seq_ids)
         Bb = self.bucket(B)
         if Bb not in self._graphs:
             self._graphs[Bb] = self._capture(Bb)
         g, st = self._graphs[Bb]
-        self._stage(st, token_ids, seq_ids, positions, seq_lens)
+        self._stage(st, token_ids, seq_ids, positions, seq_lens, src)
         g.replay()
         return st.logits[:B]
 

@@ -8,11 +8,11 @@ reference's single-device engine, engine/llm_engine.py:146-205, replicated).
 Block ids are rank-local, so each rank's slotting is exactly the reference's
 for the requests it owns.
 
-The only collective is one ``all_gather_into_tensor`` per step of a small
-int32 record per rank -- (global request id, sampled token, finished) for
-every sequence that produced a token, plus a "work left" flag -- used to
-assemble outputs on every rank and to end the loop on all ranks at the same
-step.  Over NCCL the record is a device tensor (NVLink/NVSwitch); over gloo
+The only collective is one ``all_gather_into_tensor`` per ``gather_every``
+steps of a small int32 record per rank -- (global request id, sampled token,
+finished) for every sequence that produced a token, plus a "work left" flag
+-- used to assemble outputs on every rank and to end the loop on all ranks
+at the same step.  Over NCCL the record is a device tensor (NVLink/NVSwitch); over gloo
 (CPU tests) a host tensor.  Every rank takes the same number of collective
 steps, including ranks whose shard is already finished, so no rank waits on
 a collective the others never enter.
@@ -78,6 +78,14 @@ class ShardedEngine:
     ``1 + 3 * capacity * k`` int32).  The ranks run in lockstep only at the
     gathers, so a step that is long on one rank (a chunked prefill) and short
     on another is no longer paid as the slower of the two every step.
+
+    The gathers do not stop the local loop: gather g is issued without
+    waiting (over NCCL on a side stream, so it waits for no engine work) and
+    read back at gather g + 1, by which time it has normally completed.  A
+    rank that is ahead runs its next k steps instead of idling while a slower
+    rank catches up; only when the whole run is imbalanced does one rank wait.
+    The price is that the end of the run is seen one gather late: every rank
+    stops at the gather after the one that showed all ranks done.
     """
 
     def __init__(self, engine, capacity: int | None = None, group=None,
@@ -110,6 +118,9 @@ class ShardedEngine:
         self.gather_seconds = 0.0
         self._rec = 0
         self._send = self._recv = None
+        self._issued = None  # the gather in flight: (work, recv buffer, host landing, event)
+        self._turn = 0
+        self._side = None
 
     def _size_records(self, owner: list[int]) -> None:
         if self.capacity is None:
@@ -118,8 +129,18 @@ class ShardedEngine:
                 counts[r] += 1
             self.capacity = max(1, max(counts))
         self._rec = 1 + 3 * self.capacity * self.gather_every
-        self._send = torch.empty(self._rec, dtype=torch.int32, device=self.device)
-        self._recv = torch.empty(self.world * self._rec, dtype=torch.int32, device=self.device)
+        # Two sets of buffers: gather g fills one while gather g - 1 is read from the other.
+        pin = self.device.type == "cuda"
+        self._send = [torch.empty(self._rec, dtype=torch.int32, device=self.device)
+                      for _ in range(2)]
+        self._recv = [torch.empty(self.world * self._rec, dtype=torch.int32, device=self.device)
+                      for _ in range(2)]
+        self._send_host = [torch.empty(self._rec, dtype=torch.int32, pin_memory=pin)
+                           for _ in range(2)]
+        self._recv_host = [torch.empty(self.world * self._rec, dtype=torch.int32,
+                                       pin_memory=pin) for _ in range(2)]
+        if pin:
+            self._side = torch.cuda.Stream(self.device)
 
     def add_requests(self, prompts: list, params: list) -> list[int]:
         """Shard ``prompts`` over the ranks; this rank queues its own share.
@@ -143,10 +164,9 @@ class ShardedEngine:
 
     def step(self, force_gather: bool = False) -> bool:
         """One local engine step; every ``gather_every`` calls (or when forced:
-        every rank must pass the same value) the token gather.  Returns False
-        once a gather shows every rank done."""
-        import torch.distributed as dist
-
+        every rank must pass the same value) a token gather.  Returns False
+        once the ranks have seen a gather show every rank done; a forced
+        gather is also read back at once (nothing left in flight)."""
         if self._send is None:
             self._size_records([])
         t0 = time.perf_counter()
@@ -161,19 +181,55 @@ class ShardedEngine:
         self.steps += 1
         if not force_gather and self.steps % self.gather_every:
             return True
+        earlier = self._issued
+        self._issue()
+        more = self._collect(earlier) if earlier is not None else True
+        if force_gather or not more:
+            more = self._collect(self._issued)
+            self._issued = None
+        self.gather_seconds += time.perf_counter() - t1
+        return more
+
+    def _issue(self) -> None:
+        """Start a gather of this rank's record; it is read back by ``_collect``."""
+        import torch.distributed as dist
+
+        j = self._turn
+        self._turn ^= 1
         # The record is built and read as numpy arrays: element-wise torch
         # indexing cost ~3 ms per step at 256 sequences per rank.
-        rec = np.full(self._rec, -1, dtype=np.int32)
+        rec = self._send_host[j].numpy()
+        rec[:] = -1
         rec[0] = 0 if self.engine.is_finished() else 1
         n = len(self._pending)
         if n:
             rec[1:1 + 3 * n] = np.asarray(self._pending, dtype=np.int32).reshape(-1)
         self._pending.clear()
-        self._send.copy_(torch.from_numpy(rec), non_blocking=False)
-        dist.all_gather_into_tensor(self._recv, self._send, group=self.group)
-        allrec = self._recv.view(self.world, self._rec).cpu().numpy()
+        send, recv = self._send[j], self._recv[j]
+        if self._side is None:  # host tensors (gloo)
+            work = dist.all_gather_into_tensor(recv, self._send_host[j], group=self.group,
+                                               async_op=True)
+            self._issued = (work, recv, None, None)
+            return
+        with torch.cuda.stream(self._side):
+            send.copy_(self._send_host[j], non_blocking=True)
+            work = dist.all_gather_into_tensor(recv, send, group=self.group, async_op=True)
+            work.wait()  # the side stream waits for the collective
+            self._recv_host[j].copy_(recv, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record()
+        self._issued = (work, recv, self._recv_host[j], done)
+
+    def _collect(self, issued) -> bool:
+        """Wait for a gather issued earlier and apply its tokens; whether any rank had work."""
+        work, recv, host, done = issued
+        if done is None:
+            work.wait()
+            allrec = recv.view(self.world, self._rec).numpy()
+        else:
+            done.synchronize()
+            allrec = host.view(self.world, self._rec).numpy()
         self.gathers += 1
-        self.gather_seconds += time.perf_counter() - t1
         more = bool((allrec[:, 0] > 0).any())
         slots = (self._rec - 1) // 3
         for r in range(self.world):

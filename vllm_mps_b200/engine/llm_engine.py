@@ -21,6 +21,18 @@ Per step the decode batch runs every layer with one fused sm_100a attention
 kernel; on CUDA the step is a CUDA graph captured per batch bucket
 (``engine/decode_graph.py``, ``cuda_graphs=True``), else an eager HF forward.
 Greedy sampling of the whole batch is one device argmax and one host copy.
+
+``pipeline=True`` (CUDA graphs of a Llama-family model) takes the host out of
+the GPU's critical path.  A sequence finishes only on ``max_tokens`` (the
+reference has no other stop rule, core/sequence.py:103-113), so which
+sequences run in step k+1, with which slots, is known before step k's token
+values are.  ``step()`` therefore schedules and launches step k+1 -- its
+input token for a sequence that ran in step k is read on the device from
+the ids step k's sampler left there -- and only then waits for step k's ids
+and returns step k's outputs.  While the host waits, reads back and
+schedules, the GPU already runs the next step.  Scheduling decisions, slots
+and tokens are those of the synchronous loop; each ``step()`` returns the
+outputs of the step launched by the call before it.
 """
 
 from __future__ import annotations
@@ -28,6 +40,7 @@ from __future__ import annotations
 import logging
 import time
 from dataclasses import dataclass, field
+from types import SimpleNamespace
 
 import torch
 
@@ -84,7 +97,8 @@ class LLMEngine:
                    swap: bool = False, preempt_watermark: float | None = None,
                    dtype: torch.dtype | None = None,
                    device: torch.device | str | None = None,
-                   max_prefill_rows: int = 8192, cuda_graphs: bool = True) -> "LLMEngine":
+                   max_prefill_rows: int = 8192, cuda_graphs: bool = True,
+                   pipeline: bool = False) -> "LLMEngine":
         from vllm_mps_b200.models.llama_adapter import LlamaAdapter
 
         if mode not in ("compat", "physical"):
@@ -124,6 +138,16 @@ class LLMEngine:
 
             max_blocks = (max(cfg.max_seq_len, 1) + BLOCK_SIZE - 1) // BLOCK_SIZE + 1
             eng._graphs = DecodeGraphRunner(eng.adapter, kv, BLOCK_SIZE, max_blocks)
+        eng.pipeline = bool(pipeline)
+        eng._inflight = None
+        if eng.pipeline:
+            if eng._graphs is None or not eng._graphs.fused:
+                raise ValueError("pipeline=True needs CUDA graphs of a Llama-family model")
+            # Two pinned landing buffers for the sampled ids, used in turn.
+            eng._ids_host = [torch.zeros(len(eng._graphs.prev_tokens), dtype=torch.long)
+                             .pin_memory() for _ in range(2)]
+            eng._ids_ready = [torch.cuda.Event() for _ in range(2)]
+            eng._ids_turn = 0
         eng.total_tokens_generated = 0
         eng.start_time = time.time()
         return eng
@@ -160,7 +184,118 @@ class LLMEngine:
     # ── stepping ─────────────────────────────────────────────────────────────
 
     def step(self) -> list[RequestOutput]:
-        """One scheduling + decode step over every running sequence (:286-346)."""
+        """One scheduling + decode step over every running sequence (:286-346).
+
+        With ``pipeline=True`` this launches the next step and returns the
+        outputs of the one launched before it (module docstring)."""
+        if self.pipeline:
+            return self._step_pipelined()
+        seqs = self._schedule()
+        if not seqs:
+            return []
+        seq_ids = [s.seq_id for s in seqs]
+        token_ids = [s.get_last_token_id() for s in seqs]
+        positions = [s.get_total_len() - 1 for s in seqs]
+        seq_lens = [s.get_total_len() for s in seqs]
+        if self._graphs is not None and self._graphs.can_run(seq_ids):
+            logits = self._graphs.run(token_ids, seq_ids, positions, seq_lens)
+        else:
+            logits = self.adapter.forward_batch(token_ids, seq_ids, positions, seq_lens)
+        next_tokens = self.sampler.sample_rows(
+            logits, [self._seq_to_params.get(sid, SamplingParams()) for sid in seq_ids])
+        return self._update_sequences(seq_ids, next_tokens)
+
+    def _step_pipelined(self) -> list[RequestOutput]:
+        seqs = self._schedule()
+        if not seqs:
+            return self._resolve()
+        seq_ids = [s.seq_id for s in seqs]
+        positions = [s.get_total_len() - 1 for s in seqs]
+        seq_lens = [s.get_total_len() for s in seqs]
+        params = [self._seq_to_params.get(sid, SamplingParams()) for sid in seq_ids]
+        g = self._graphs
+        if not g.can_run(seq_ids):
+            # The eager forward takes host token ids: settle the step in flight
+            # first.  This step's ids are then known at once, but they are
+            # still reported by the next call, so that every call returns one
+            # step (a RequestOutput is updated in place: two steps of one
+            # request in one return would both show the later token).
+            done = self._resolve()
+            token_ids = [s.get_last_token_id() for s in seqs]
+            logits = self.adapter.forward_batch(token_ids, seq_ids, positions, seq_lens)
+            ids = self.sampler.sample_rows(logits, params)
+            self._inflight = self._book(seqs, ids, rows={}, host=None, ready=None)
+            return done
+        # A sequence of the step in flight has a placeholder as its last token;
+        # its input is that step's sampled id, at the row it had there.
+        rows = self._inflight.rows if self._inflight is not None else {}
+        src = [rows.get(sid, -1) for sid in seq_ids]
+        token_ids = [0 if r >= 0 else s.token_ids[-1] for s, r in zip(seqs, src)]
+        logits = g.run(token_ids, seq_ids, positions, seq_lens, src=src)
+        B = len(seqs)
+        ids = g.prev_tokens[:B]
+        self.sampler.sample_rows_device(logits, params, out=ids)
+        j = self._ids_turn
+        self._ids_turn ^= 1
+        self._ids_host[j][:B].copy_(ids, non_blocking=True)
+        self._ids_ready[j].record()
+        # Book the step now with placeholder ids (lengths and finishes do not
+        # depend on the values), so the next schedule sees the same state as
+        # after a synchronous step.
+        launched = self._book(seqs, [-1] * B, rows={sid: i for i, sid in enumerate(seq_ids)},
+                              host=self._ids_host[j], ready=self._ids_ready[j])
+        done = self._resolve()
+        self._inflight = launched
+        return done
+
+    def _book(self, seqs, ids, rows, host, ready) -> SimpleNamespace:
+        """Append one id per sequence (placeholders when ``host`` is given) and
+        retire the sequences that reach ``max_tokens``; the step's record."""
+        booked = []
+        for s, t in zip(seqs, ids):
+            booked.append((s, len(s.token_ids)))
+            s.add_token(t)
+            if s.is_finished():
+                self._retire(s.seq_id)
+        return SimpleNamespace(booked=booked, rows=rows, host=host, ready=ready,
+                               ids=None if host is not None else list(ids))
+
+    def _resolve(self) -> list[RequestOutput]:
+        """Wait for the step in flight's ids, write them over its placeholders."""
+        fl = self._inflight
+        if fl is None:
+            return []
+        self._inflight = None
+        if fl.ids is not None:
+            ids = fl.ids
+        else:
+            fl.ready.synchronize()
+            ids = fl.host[:len(fl.booked)].numpy().tolist()
+        updated = []
+        for (seq, at), token_id in zip(fl.booked, ids):
+            seq.token_ids[at] = token_id
+            self.total_tokens_generated += 1
+            request_id = self._seq_to_request.get(seq.seq_id)
+            if request_id is None:
+                continue
+            out = self._outputs[request_id]
+            out.token_ids.append(token_id)
+            if self.tokenizer is not None:
+                out.generated_text = self.tokenizer.decode(seq.token_ids[seq.prompt_len:at + 1],
+                                                           skip_special_tokens=True)
+            out.finished = at + 1 - seq.prompt_len >= seq.sampling_params.max_tokens
+            out.num_steps += 1
+            updated.append(out)
+        return updated
+
+    def _retire(self, seq_id: int) -> None:
+        self.scheduler.mark_finished(seq_id)
+        self._prefilled.discard(seq_id)
+        for pl in self.adapter.paged_layers:
+            pl.evict_sequence(seq_id)
+
+    def _schedule(self) -> list[Sequence]:
+        """Schedule a step; give every sequence its slots; prefill what needs it."""
         sched_out = self.scheduler.schedule()
         for group in sched_out.preempted_groups:
             for s in group.sequences:
@@ -184,17 +319,7 @@ class LLMEngine:
                 kv.append_slots(s.seq_id, short)
         if self.mode == "physical":
             self._prefill([s for s in seqs if s.seq_id not in self._prefilled])
-        seq_ids = [s.seq_id for s in seqs]
-        token_ids = [s.get_last_token_id() for s in seqs]
-        positions = [s.get_total_len() - 1 for s in seqs]
-        seq_lens = [s.get_total_len() for s in seqs]
-        if self._graphs is not None and self._graphs.can_run(seq_ids):
-            logits = self._graphs.run(token_ids, seq_ids, positions, seq_lens)
-        else:
-            logits = self.adapter.forward_batch(token_ids, seq_ids, positions, seq_lens)
-        next_tokens = self.sampler.sample_rows(
-            logits, [self._seq_to_params.get(sid, SamplingParams()) for sid in seq_ids])
-        return self._update_sequences(seq_ids, next_tokens)
+        return seqs
 
     def _prefill(self, seqs: list[Sequence]) -> None:
         """Write the K/V of every token but the last of each sequence, all layers.
@@ -256,10 +381,7 @@ class LLMEngine:
             seq.add_token(token_id)
             self.total_tokens_generated += 1
             if seq.is_finished():
-                self.scheduler.mark_finished(seq_id)
-                self._prefilled.discard(seq_id)
-                for pl in self.adapter.paged_layers:
-                    pl.evict_sequence(seq_id)
+                self._retire(seq_id)
             out = self._outputs[request_id]
             out.token_ids.append(token_id)  # mirrors seq.output_token_ids
             if self.tokenizer is not None:
@@ -286,7 +408,7 @@ class LLMEngine:
 
     def is_finished(self) -> bool:
         return (self.scheduler.get_num_waiting() == 0 and self.scheduler.get_num_running() == 0
-                and self.scheduler.get_num_preempted() == 0)
+                and self.scheduler.get_num_preempted() == 0 and self._inflight is None)
 
     def get_elapsed(self) -> float:
         return time.time() - self.start_time

@@ -53,6 +53,7 @@ EXPORTED_SYMBOLS = (
     "vmps_paged_prefill_attention",
     "vmps_add_rmsnorm",
     "vmps_silu_mul",
+    "vmps_embed_rmsnorm",
     "vmps_decode_gemm_supported",
     "vmps_decode_gemm",
     "vmps_stage_copy",
@@ -104,6 +105,9 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.vmps_add_rmsnorm.argtypes = [vp, i64, vp, i64, vp, i64, vp, i32, i32, f32, i32, vp]
         lib.vmps_silu_mul.restype = i32
         lib.vmps_silu_mul.argtypes = [vp, i64, vp, i64, i32, i32, i32, vp]
+        lib.vmps_embed_rmsnorm.restype = i32
+        lib.vmps_embed_rmsnorm.argtypes = [vp, i64, vp, i64, vp, i64, vp, vp, vp, i32, vp, i32,
+                                           i32, f32, i32, vp]
         lib.vmps_decode_gemm_supported.restype = i32
         lib.vmps_decode_gemm_supported.argtypes = [i32, i32, i32, i32]
         lib.vmps_decode_gemm.restype = i32
@@ -459,6 +463,53 @@ def add_rmsnorm(residual: torch.Tensor, weight: torch.Tensor, eps: float,
                                   dtype_code(residual.dtype), _stream(dev))
     _check(rc, "add_rmsnorm")
     return out
+
+
+def embed_rmsnorm(table: torch.Tensor, weight: torch.Tensor, eps: float, tokens: torch.Tensor,
+                  src: torch.Tensor | None = None, prev: torch.Tensor | None = None,
+                  residual: torch.Tensor | None = None,
+                  out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Embedding rows of the step's tokens and the first RMSNorm, one kernel.
+
+    Row i's token is ``prev[src[i]]`` when ``src`` is given and ``src[i] >=
+    0``, else ``tokens[i]`` (``tokens``/``src`` int32, ``prev`` int64: the
+    previous step's sampled ids, still on the device).  ``residual[i] =
+    table[token]`` (the embedding lookup) and ``out = RMSNorm(residual) *
+    weight`` with :func:`add_rmsnorm`'s rounding.  A ``src`` entry beyond
+    ``prev`` or a token outside the table sets bit 128 of the device error
+    word and zeroes the row.  Returns ``(residual, out)``.
+    """
+    vocab, hidden = table.shape
+    rows = tokens.numel()
+    if tokens.dtype != torch.int32 or not tokens.is_contiguous():
+        raise ValueError("tokens must be contiguous int32")
+    if (src is None) != (prev is None):
+        raise ValueError("src and prev go together")
+    if src is not None:
+        if src.dtype != torch.int32 or not src.is_contiguous() or src.numel() != rows:
+            raise ValueError("src must be contiguous int32 with one entry per token")
+        if prev.dtype != torch.int64 or not prev.is_contiguous():
+            raise ValueError("prev must be contiguous int64")
+    if not table.is_contiguous() or weight.dtype != table.dtype or not weight.is_contiguous() \
+            or weight.numel() != hidden:
+        raise ValueError("table and weight must be contiguous, same dtype, weight (hidden,)")
+    if residual is None:
+        residual = torch.empty((rows, hidden), dtype=table.dtype, device=table.device)
+    if out is None:
+        out = torch.empty_like(residual)
+    for t, name in ((residual, "residual"), (out, "out")):
+        if t.shape != (rows, hidden) or t.dtype != table.dtype:
+            raise ValueError(f"{name} must be ({rows}, {hidden}) {table.dtype}")
+    dev = _require_cuda(table, weight, tokens, src, prev, residual, out)
+    lib = load_library()
+    with torch.cuda.device(dev):
+        rc = lib.vmps_embed_rmsnorm(_ptr(out), _row_stride(out, hidden, "out"), _ptr(residual),
+                                    _row_stride(residual, hidden, "residual"), _ptr(table), vocab,
+                                    _ptr(tokens), _ptr(src), _ptr(prev),
+                                    0 if prev is None else prev.numel(), _ptr(weight), rows,
+                                    hidden, float(eps), dtype_code(table.dtype), _stream(dev))
+    _check(rc, "embed_rmsnorm")
+    return residual, out
 
 
 def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

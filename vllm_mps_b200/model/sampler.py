@@ -67,14 +67,24 @@ class Sampler:
         Rows with ``temperature > 0`` are filtered (``_sorted_filtered``) and
         sampled together on the device from the softmax of what is left.
         """
-        B = logits.size(0)
-        if B == 0:
+        if logits.size(0) == 0:
             return []
-        out = torch.argmax(logits, dim=-1)
+        return self.sample_rows_device(logits, params, generator).tolist()
+
+    def sample_rows_device(self, logits: torch.Tensor, params: list[SamplingParams],
+                           generator: torch.Generator | None = None,
+                           out: torch.Tensor | None = None) -> torch.Tensor:
+        """:meth:`sample_rows` without the device-to-host read: int64 ids on the device.
+
+        ``out`` (int64, ``(B,)``, on the logits' device) receives the ids when
+        given; a pipelined engine passes the buffer its next step reads them
+        from.  Nothing here waits for the GPU when every row is greedy.
+        """
+        out = torch.argmax(logits, dim=-1, out=out)
         rows = [i for i, p in enumerate(params) if p.temperature != 0.0]
         if rows:
             idx = torch.tensor(rows, device=logits.device)
             sv, order = self._sorted_filtered(logits[idx], [params[i] for i in rows])
             pick = torch.multinomial(F.softmax(sv, dim=-1), 1, generator=generator)
             out[idx] = order.gather(1, pick)[:, 0].to(out.dtype)
-        return out.tolist()
+        return out
