@@ -984,9 +984,14 @@ def c4_leg(args, rank, world, local_rank, n_req=1024):
     if world > 1:
         import torch.distributed as dist
     eng.capture_decode_graphs()  # startup work: every batch bucket up to 256
-    # Warm-up: a few requests through this rank's engine (workspaces, prefill path).
+    # Warm-up: a few requests through this rank's engine (workspaces, prefill
+    # path), one of them a full 16384-row prefill chunk so that the chunk-sized
+    # activations and GEMM shapes are set up before the timed region.
     for p in prompts[:4]:
         eng.add_request(p[:64], SamplingParams(temperature=0.0, max_tokens=8))
+    for i in range(4):
+        eng.add_request(rng.integers(0, vocab, size=4097).tolist(),
+                        SamplingParams(temperature=0.0, max_tokens=2))
     while not eng.is_finished():
         eng.step()
     torch.cuda.synchronize(dev)

@@ -389,3 +389,35 @@ def test_graph_decode_matches_eager_decode():
                 top2 = torch.topk(le[t][i], 2).values
                 assert float(top2[0] - top2[1]) < 2e-2, (i, t)
                 break
+
+
+def test_fused_prefill_writes_the_hf_prefill_kv():
+    """Physical-mode prefill through ``DecodeGraphRunner.prefill_rows`` (the
+    fused layer sequence, no HF forward, the last layer only writing K/V)
+    writes the same K/V as the HF-forward prefill (``cuda_graphs=False``),
+    up to the GEMM shapes' fp32 summation order, in every layer."""
+    from vllm_mps_b200.core.sequence import SamplingParams
+    from vllm_mps_b200.engine.llm_engine import LLMEngine
+
+    rng = np.random.default_rng(12)
+    prompts = [rng.integers(0, 1024, size=n).tolist() for n in (2, 17, 300, 64, 129)]
+    pools = {}
+    for graphs in (True, False):
+        eng = LLMEngine.from_model(_small_llama(seed=6), num_gpu_blocks=64, num_cpu_blocks=8,
+                                   max_batch_size=8, max_tokens_per_step=10 ** 6,
+                                   mode="physical", device="cuda", cuda_graphs=graphs,
+                                   max_prefill_rows=200)
+        assert (eng._graphs is not None and eng._graphs.fused) == graphs
+        for p in prompts:
+            eng.add_request(p, SamplingParams(temperature=0.0, max_tokens=1))
+        seqs = [eng._seqs[i] for i in range(len(prompts))]
+        eng.scheduler.schedule()  # admit all, reserve the prompt slots
+        eng._prefill(seqs)
+        torch.cuda.synchronize()
+        pools[graphs] = eng.memory_pool._all.float().clone()
+    a, b = pools[True], pools[False]
+    assert a.abs().sum() > 0
+    # Slots of every prompt token but the last were written, the same ones in both.
+    assert torch.equal((a != 0).flatten(-2).any(-1), (b != 0).flatten(-2).any(-1))
+    torch.testing.assert_close(a, b, atol=2e-2, rtol=2e-2)
+    assert (a - b).abs().mean().item() < 1e-3

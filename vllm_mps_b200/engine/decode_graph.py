@@ -198,6 +198,42 @@ class DecodeGraphRunner:
         else:
             st.logits.copy_(head(h))
 
+    def prefill_rows(self, tokens: torch.Tensor, meta) -> None:
+        """Write every layer's K/V for the prompt rows of one prefill chunk.
+
+        The fused Llama layer sequence of the decode step, eager and at the
+        chunk's row count: ``embed_rmsnorm``, then per layer kernel 1 + kernel
+        3 (``PagedAttentionLayer._prefill_rows``), residual add + RMSNorm, the
+        [gate | up] GEMM, SiLU * up, the down GEMM and residual add + the next
+        RMSNorm; the last layer only projects and writes its K/V (nothing
+        reads its attention or MLP output).  Unlike the HF forward it builds
+        no causal mask (transformers' mask helpers read the device, a stall
+        per chunk) and no rotary table.  ``tokens``: int32 (rows,) on the
+        device; ``meta``: ``build_prefill_metadata`` of the chunk.
+        """
+        from vllm_mps_b200 import kernels as K
+
+        if self._gate_up is None:
+            raise ValueError("prefill_rows needs the fused Llama layer sequence")
+        m = self.adapter.hf_model
+        layers = m.model.layers
+        first = layers[0].input_layernorm
+        res, h = K.embed_rmsnorm(m.model.embed_tokens.weight, first.weight,
+                                 first.variance_epsilon, tokens)
+        last = len(layers) - 1
+        for i, layer in enumerate(layers):
+            if i == last:
+                layer.self_attn._write_kv_rows(h, meta)
+                break
+            attn = layer.self_attn._prefill_rows(h.unsqueeze(1), meta)
+            post = layer.post_attention_layernorm
+            K.add_rmsnorm(res, post.weight, post.variance_epsilon, delta=attn.view_as(res), out=h)
+            act = K.silu_mul(torch.matmul(h, self._gate_up[i].t()))
+            down = layer.mlp.down_proj
+            mlp_out = torch.matmul(act, down.weight.t()) if down.bias is None else down(act)
+            nxt = layers[i + 1].input_layernorm
+            K.add_rmsnorm(res, nxt.weight, nxt.variance_epsilon, delta=mlp_out, out=h)
+
     def _static(self, Bb: int):
         """Static buffers of a bucket:
         [tables Bb x W | lengths | positions | slots | tokens | token sources]."""

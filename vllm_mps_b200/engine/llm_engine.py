@@ -329,7 +329,9 @@ class LLMEngine:
         attending to the earlier ones through the pool).  Per layer, kernel 1
         writes every row's rotated K and V, then kernel 3 (tcgen05 causal
         prefill) computes each row against its sequence's slots
-        ``0..position``.
+        ``0..position``.  With the CUDA-graph runner's fused Llama layers the
+        chunk runs through ``DecodeGraphRunner.prefill_rows`` (no HF forward),
+        else through the HF model with the paged attention layers.
         """
         pieces, rows = [], 0
         for s in seqs:
@@ -355,6 +357,11 @@ class LLMEngine:
                                          [(s.seq_id, qs, ql) for s, qs, ql in pieces],
                                          BLOCK_SIZE, dev)
         toks = [t for s, qs, ql in pieces for t in s.token_ids[qs:qs + ql]]
+        if self._graphs is not None and self._graphs.fused:
+            tok = torch.tensor(toks, dtype=torch.int32).pin_memory()
+            with torch.no_grad():
+                self._graphs.prefill_rows(tok.to(dev, non_blocking=True), meta)
+            return
         tok = torch.tensor(toks, dtype=torch.long)
         if dev.type == "cuda":
             tok = tok.pin_memory()

@@ -155,6 +155,19 @@ class PagedAttentionLayer(nn.Module):
                                       scale=1.0 / math.sqrt(D))
         return self.W_O(out.view(B, 1, n_q * D))
 
+    def _write_kv_rows(self, hidden_states: torch.Tensor, meta) -> None:
+        """Only the K/V half of :meth:`_prefill_rows`: the K and V projections
+        and kernel 1's write of every row's rotated K and V (no query, no
+        attention).  The last layer of a prefill needs nothing more: no later
+        layer reads its output."""
+        from vllm_mps_b200.kernels import rope_reshape_and_cache
+
+        B = hidden_states.shape[0]
+        n_q, n_kv, D = self.n_heads, self.n_kv_heads, self.d_k
+        kv = torch.matmul(hidden_states.reshape(B, self.d_model), self._w_qkv[n_q * D:].t())
+        rope_reshape_and_cache(None, kv[:, : n_kv * D], kv[:, n_kv * D:], meta.pos_tensor,
+                               meta.slot_mapping, self.rotary_emb.inv_freq, self._pool())
+
     def _forward_batch(self, hidden_states: torch.Tensor, seq_ids: list[int],
                        positions: list[int], seq_lens: list[int]):
         """Batched decode, one token per sequence (:245-364); prompt rows in prefill."""
