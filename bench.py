@@ -984,13 +984,18 @@ def c4_leg(args, rank, world, local_rank, n_req=1024):
     if world > 1:
         import torch.distributed as dist
     eng.capture_decode_graphs()  # startup work: every batch bucket up to 256
-    # Warm-up: a few requests through this rank's engine (workspaces, prefill
-    # path), one of them a full 16384-row prefill chunk so that the chunk-sized
-    # activations and GEMM shapes are set up before the timed region.
-    for p in prompts[:4]:
-        eng.add_request(p[:64], SamplingParams(temperature=0.0, max_tokens=8))
+    eng.warm_prefill_gemms()     # startup work: every padded prefill GEMM row count
+    # Warm-up through this rank's engine, untimed: 64 requests of the same
+    # length distribution (other seeded ids) with short outputs, so that the
+    # prefill chunk shapes, batch buckets, workspaces and the allocator's
+    # blocks of the timed run are set up before it, plus one full 16384-row
+    # prefill chunk.
+    wrng = np.random.default_rng(5)
+    for n in np.clip(np.round(wrng.lognormal(6, 1, 64)), 16, 4096).astype(int):
+        eng.add_request(wrng.integers(0, vocab, size=int(n)).tolist(),
+                        SamplingParams(temperature=0.0, max_tokens=16))
     for i in range(4):
-        eng.add_request(rng.integers(0, vocab, size=4097).tolist(),
+        eng.add_request(wrng.integers(0, vocab, size=4097).tolist(),
                         SamplingParams(temperature=0.0, max_tokens=2))
     while not eng.is_finished():
         eng.step()

@@ -393,9 +393,10 @@ def test_graph_decode_matches_eager_decode():
 
 def test_fused_prefill_writes_the_hf_prefill_kv():
     """Physical-mode prefill through ``DecodeGraphRunner.prefill_rows`` (the
-    fused layer sequence, no HF forward, the last layer only writing K/V)
-    writes the same K/V as the HF-forward prefill (``cuda_graphs=False``),
-    up to the GEMM shapes' fp32 summation order, in every layer."""
+    fused layer sequence, no HF forward, GEMM rows padded to a multiple of
+    128, the last layer only writing K/V) writes the same K/V as the
+    HF-forward prefill (``cuda_graphs=False``), up to the GEMM shapes' fp32
+    summation order, in every layer."""
     from vllm_mps_b200.core.sequence import SamplingParams
     from vllm_mps_b200.engine.llm_engine import LLMEngine
 
@@ -408,6 +409,8 @@ def test_fused_prefill_writes_the_hf_prefill_kv():
                                    mode="physical", device="cuda", cuda_graphs=graphs,
                                    max_prefill_rows=200)
         assert (eng._graphs is not None and eng._graphs.fused) == graphs
+        # Row counts 128 and 256 (chunks of up to 200 rows, padded to 128).
+        assert eng.warm_prefill_gemms() == (2 if graphs else 0)
         for p in prompts:
             eng.add_request(p, SamplingParams(temperature=0.0, max_tokens=1))
         seqs = [eng._seqs[i] for i in range(len(prompts))]

@@ -48,6 +48,13 @@ import torch
 logger = logging.getLogger(__name__)
 
 BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256, 512)
+# Prefill chunks run their GEMMs on a row count rounded up to this multiple:
+# cuBLAS spends ~1 ms of host time choosing a kernel the first time it sees
+# a shape (then ~20 us), so a serving run whose chunks all differ in length
+# would pay that per chunk and GEMM; rounded, a run meets at most
+# max_prefill_rows / 128 row counts, and ``warm_prefill_gemms`` can meet
+# them all at startup.
+PREFILL_ROW_ALIGN = 128
 
 
 class DecodeGraphRunner:
@@ -208,8 +215,10 @@ class DecodeGraphRunner:
         RMSNorm; the last layer only projects and writes its K/V (nothing
         reads its attention or MLP output).  Unlike the HF forward it builds
         no causal mask (transformers' mask helpers read the device, a stall
-        per chunk) and no rotary table.  ``tokens``: int32 (rows,) on the
-        device; ``meta``: ``build_prefill_metadata`` of the chunk.
+        per chunk) and no rotary table.  ``tokens``: int32 on the device,
+        the chunk's ``meta.rows`` ids followed by any padding (the GEMMs run
+        on every row; ``padded_rows`` gives the engine's row count);
+        ``meta``: ``build_prefill_metadata`` of the chunk.
         """
         from vllm_mps_b200 import kernels as K
 
@@ -233,6 +242,37 @@ class DecodeGraphRunner:
             mlp_out = torch.matmul(act, down.weight.t()) if down.bias is None else down(act)
             nxt = layers[i + 1].input_layernorm
             K.add_rmsnorm(res, nxt.weight, nxt.variance_epsilon, delta=mlp_out, out=h)
+
+    @staticmethod
+    def padded_rows(rows: int) -> int:
+        """GEMM row count of a prefill chunk of ``rows`` rows."""
+        return -(-rows // PREFILL_ROW_ALIGN) * PREFILL_ROW_ALIGN
+
+    def warm_prefill_gemms(self, max_rows: int) -> int:
+        """Run each prefill GEMM shape once at every padded row count up to
+        ``max_rows`` (startup work: cuBLAS then has its kernel choice for all
+        of them).  Returns the number of row counts."""
+        if self._gate_up is None:
+            return 0
+        m = self.adapter.hf_model
+        d = self.adapter.model_config.d_model
+        a0 = m.model.layers[0].self_attn
+        nq_d = a0.n_heads * a0.d_k
+        down = m.model.layers[0].mlp.down_proj.weight
+        top = self.padded_rows(max(1, max_rows))
+        # The prefill's operands, same widths (so same leading dimensions).
+        zeros = lambda cols: torch.zeros((top, cols), dtype=a0._w_qkv.dtype, device=self.device)
+        h, act, attn = zeros(d), zeros(down.shape[1]), zeros(nq_d)
+        pairs = [(h, a0._w_qkv), (h, a0._w_qkv[nq_d:]), (h, self._gate_up[0]), (act, down),
+                 (attn, a0.W_O.weight)]
+        n = 0
+        with torch.no_grad():
+            for rows in range(PREFILL_ROW_ALIGN, top + 1, PREFILL_ROW_ALIGN):
+                for x, w in pairs:
+                    torch.matmul(x[:rows], w.t())
+                n += 1
+        torch.cuda.synchronize(self.device)
+        return n
 
     def _static(self, Bb: int):
         """Static buffers of a bucket:

@@ -152,6 +152,14 @@ class LLMEngine:
         eng.start_time = time.time()
         return eng
 
+    def warm_prefill_gemms(self) -> int:
+        """Startup work for a serving run: meet every prefill GEMM shape up to
+        ``max_prefill_rows`` once (fused Llama path; returns how many row
+        counts, 0 when there is nothing to warm)."""
+        if self._graphs is None:
+            return 0
+        return self._graphs.warm_prefill_gemms(self.max_prefill_rows)
+
     def capture_decode_graphs(self) -> list[int]:
         """Capture the decode step's CUDA graph for every batch bucket up to
         ``max_batch_size`` now instead of on first use; returns the buckets."""
@@ -358,6 +366,7 @@ class LLMEngine:
                                          BLOCK_SIZE, dev)
         toks = [t for s, qs, ql in pieces for t in s.token_ids[qs:qs + ql]]
         if self._graphs is not None and self._graphs.fused:
+            toks += [0] * (self._graphs.padded_rows(len(toks)) - len(toks))
             tok = torch.tensor(toks, dtype=torch.int32).pin_memory()
             with torch.no_grad():
                 self._graphs.prefill_rows(tok.to(dev, non_blocking=True), meta)

@@ -139,20 +139,29 @@ class PagedAttentionLayer(nn.Module):
         prefill) then computes every row against its sequence's slots
         ``0..position`` -- the result of the reference's token-by-token
         single-token path (:175-241) for the whole chunk at once.
+
+        ``hidden_states`` may carry padding rows after the chunk's
+        ``meta.rows`` rows (a caller that rounds the GEMMs' row count): the
+        projections run on every row, kernels 1 and 3 on the chunk's rows
+        only, and the padding rows of the result are not meaningful.
         """
         from vllm_mps_b200.kernels import paged_prefill_attention, rope_reshape_and_cache
 
         B = hidden_states.shape[0]
+        R = meta.rows
         n_q, n_kv, D = self.n_heads, self.n_kv_heads, self.d_k
         qkv = torch.matmul(hidden_states.reshape(B, self.d_model), self._w_qkv.t())
-        q = qkv[:, : n_q * D]
-        k = qkv[:, n_q * D: (n_q + n_kv) * D]
-        v = qkv[:, (n_q + n_kv) * D:]
+        q = qkv[:R, : n_q * D]
+        k = qkv[:R, n_q * D: (n_q + n_kv) * D]
+        v = qkv[:R, (n_q + n_kv) * D:]
         rope_reshape_and_cache(q, k, v, meta.pos_tensor, meta.slot_mapping,
                                self.rotary_emb.inv_freq, self._pool())
-        out = paged_prefill_attention(q.view(B, n_q, D), self._pool(), meta.bt_tensor,
-                                      meta.q_start, meta.q_lens, meta.cu_q, meta.max_q_len,
-                                      scale=1.0 / math.sqrt(D))
+        out = torch.empty((B, n_q * D), dtype=qkv.dtype, device=qkv.device)
+        if B > R:
+            out[R:].zero_()
+        paged_prefill_attention(q.view(R, n_q, D), self._pool(), meta.bt_tensor, meta.q_start,
+                                meta.q_lens, meta.cu_q, meta.max_q_len, scale=1.0 / math.sqrt(D),
+                                out=out[:R].view(R, n_q, D))
         return self.W_O(out.view(B, 1, n_q * D))
 
     def _write_kv_rows(self, hidden_states: torch.Tensor, meta) -> None:
@@ -162,10 +171,10 @@ class PagedAttentionLayer(nn.Module):
         layer reads its output."""
         from vllm_mps_b200.kernels import rope_reshape_and_cache
 
-        B = hidden_states.shape[0]
+        B, R = hidden_states.shape[0], meta.rows
         n_q, n_kv, D = self.n_heads, self.n_kv_heads, self.d_k
         kv = torch.matmul(hidden_states.reshape(B, self.d_model), self._w_qkv[n_q * D:].t())
-        rope_reshape_and_cache(None, kv[:, : n_kv * D], kv[:, n_kv * D:], meta.pos_tensor,
+        rope_reshape_and_cache(None, kv[:R, : n_kv * D], kv[:R, n_kv * D:], meta.pos_tensor,
                                meta.slot_mapping, self.rotary_emb.inv_freq, self._pool())
 
     def _forward_batch(self, hidden_states: torch.Tensor, seq_ids: list[int],
