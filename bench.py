@@ -1241,6 +1241,157 @@ def run_gemm(args, rank, world, local_rank):
     return 0
 
 
+BGEMM_SHAPES = (
+    # name, M (batch), N (output features), K -- Llama-3-8B projections at the config-2 batch
+    ("qkv", 256, 6144, 4096),
+    ("o", 256, 4096, 4096),
+    ("gate_up", 256, 28672, 4096),
+    ("down", 256, 4096, 14336),
+)
+
+
+def run_bgemm(args, rank, world, local_rank):
+    """Kernel 5 (``kernels.batch_gemm``: tcgen05, cluster split-K) on the batch-256
+    projections of a Llama-3-8B decode step, next to cuBLAS (``torch.matmul``).
+
+    A step is one pass of the four projections; four weight sets (1.75 GB)
+    rotate so inputs are larger than L2.  Each projection is also timed alone
+    (40 launches in a CUDA graph) beside cuBLAS on the same inputs.
+    """
+    import torch
+
+    from vllm_mps_b200 import kernels as K
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    R, dt = 4, torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(7)
+    W = {n: [(torch.randn(N, Kd, generator=g, device=dev) / Kd ** 0.5).to(dt) for _ in range(R)]
+         for n, M, N, Kd in BGEMM_SHAPES}
+    X = {n: (torch.randn(M, Kd, generator=g, device=dev) * 0.5).to(dt) for n, M, N, Kd in BGEMM_SHAPES}
+    OUT = {n: torch.empty(M, N, device=dev, dtype=dt) for n, M, N, Kd in BGEMM_SHAPES}
+    flops = sum(2 * M * N * Kd for _, M, N, Kd in BGEMM_SHAPES)
+    wbytes = sum(N * Kd * 2 for _, M, N, Kd in BGEMM_SHAPES)
+
+    def capture(fns):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for f in fns:
+                f()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for f in fns:
+                f()
+        return gr
+
+    def timed(gr, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) * 1e-3
+
+    def step(r):
+        for n, *_ in BGEMM_SHAPES:
+            K.batch_gemm(X[n], W[n][r], out=OUT[n])
+
+    g_steps = capture([lambda r=r: step(r) for r in range(R)])
+    for _ in range(max(1, args.warmup // R)):
+        g_steps.replay()
+    reps = max(1, args.steps // R)
+    with ClockSampler(dev.index or 0) as clocks:
+        t = timed(g_steps, reps)
+    n_steps = reps * R
+    t_step = t / n_steps
+    per = {}
+    for n, M, N, Kd in BGEMM_SHAPES:
+        it = [0]
+
+        def ours(n=n):
+            it[0] = (it[0] + 1) % R
+            K.batch_gemm(X[n], W[n][it[0]], out=OUT[n])
+
+        def cublas(n=n):
+            it[0] = (it[0] + 1) % R
+            torch.matmul(X[n], W[n][it[0]].t(), out=OUT[n])
+
+        a, b = capture([ours] * 40), capture([cublas] * 40)
+        timed(a, 2), timed(b, 2)
+        ta, tb = timed(a, 5) / 200, timed(b, 5) / 200
+        per[n] = {"M": M, "N": N, "K": Kd, "split": K.batch_gemm_split(M, N, Kd),
+                  "us": round(ta * 1e6, 2), "tflops": round(2 * M * N * Kd / ta / 1e12, 1),
+                  "cublas_us": round(tb * 1e6, 2)}
+    # End to end: every step's X in from pinned host memory, the outputs back.
+    xh = {n: X[n].cpu().pin_memory() for n in X}
+    oh = {n: torch.empty(OUT[n].shape, dtype=dt).pin_memory() for n in OUT}
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = min(n_steps, 100)
+    e0.record()
+    for i in range(n_e2e):
+        for n in X:
+            X[n].copy_(xh[n], non_blocking=True)
+        step(i % R)
+        for n in OUT:
+            oh[n].copy_(OUT[n], non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t_e2e = e0.elapsed_time(e1) * 1e-3 / n_e2e
+    if K.error_word(dev):
+        raise RuntimeError("device error word set during the batch-GEMM run")
+    if rank == 0:
+        import torch as _t
+
+        _t.set_num_threads(os.cpu_count() or 1)
+        wc = {n: W[n][0][:1024].float().cpu() for n in W}  # a bounded sample: 1024 rows each
+        xc = {n: X[n].float().cpu() for n in X}
+        t0, n_cpu = time.perf_counter(), 0
+        while time.perf_counter() - t0 < 5.0 and n_cpu < 20:
+            for n in W:
+                xc[n] @ wc[n].t()
+            n_cpu += 1
+        t_cpu = (time.perf_counter() - t0) / n_cpu
+        cpu_flops = sum(2 * X[n].shape[0] * 1024 * X[n].shape[1] for n in W)
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peak = (float(json.load(f)["bf16_tflops"]), "measured (burst)")
+        except Exception:
+            peak = (1590.0, "fallback")
+        achieved = flops / t_step / 1e12
+        line = {
+            "metric": "batch-GEMM throughput", "value": achieved, "unit": "TFLOP/s", "n_gpus": 1,
+            "steps": n_steps, "warmup": args.warmup, "ms_per_step": t_step * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1)/sqrt(K) weights, N(0,0.25) activations)",
+            "config": {"workload": "Llama-3-8B decode projections at batch 256 (QKV, O, [gate;up], "
+                                   "down) through kernels.batch_gemm",
+                       "global_batch": 256, "weight_bytes_per_step": wbytes,
+                       "l2": "inputs larger than L2: 4 weight sets (1.75 GB) rotated",
+                       "per_projection": per},
+            "e2e": {"value": flops / t_e2e / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": sum(x.numel() * 2 for x in X.values()),
+                    "d2h_bytes_per_step": sum(o.numel() * 2 for o in OUT.values()),
+                    "api": "kernels.batch_gemm; per step X in from pinned memory, outputs back"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak[0],
+                         "unit": "TFLOP/s", "frac": achieved / peak[0], "traffic": None,
+                         "peak_kind": peak[1], "kernel": "batch_gemm_kernel (4 projections)",
+                         "hbm_gb_s": wbytes / t_step / 1e9},
+            "clocks": clocks.summary(),
+            "gpu_launches": n_steps * len(BGEMM_SHAPES),
+            "cpu_baseline": {"value": cpu_flops / t_cpu / 1e12, "unit": "TFLOP/s",
+                             "cores": _t.get_num_threads(), "kind": "port",
+                             "sample": f"{n_cpu} passes of the four projections on 1024 output "
+                                       "features each, torch float32 matmul on the host cores"},
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def _summary(rec):
     """The keys of a leg's record that a sub-record keeps."""
     keep = ("metric", "value", "unit", "steps", "gathers", "ms_per_step", "scaling", "dtype",
@@ -1289,7 +1440,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config",
-                    choices=sorted(CONFIGS) + sorted(PREFILL) + sorted(ENGINE) + ["c4", "gemm"],
+                    choices=sorted(CONFIGS) + sorted(PREFILL) + sorted(ENGINE)
+                    + ["c4", "gemm", "bgemm"],
                     default="c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-subrecords", action="store_true",
@@ -1305,10 +1457,10 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference" and cfg is not None:
         return run_reference(args, cfg, rank, world)
-    if args.impl == "reference" and (args.config in ENGINE or args.config in ("c4", "gemm")):
+    if args.impl == "reference" and (args.config in ENGINE or args.config in ("c4", "gemm", "bgemm")):
         why = ("the reference engine is Python on its CPU path and does not travel to the GPU box; "
                "see the c1/c3/prefill reference lines")
-        if args.config == "gemm":
+        if args.config in ("gemm", "bgemm"):
             why = ("the reference runs these projections as nn.Linear inside its CPU engine; the "
                    "ours-line's cpu_baseline times them as torch float32 matmuls on the host cores")
         if rank == 0:
@@ -1328,6 +1480,8 @@ def main():
             return run_c4(args, rank, world, local_rank)
         if args.config == "gemm":
             return run_gemm(args, rank, world, local_rank)
+        if args.config == "bgemm":
+            return run_bgemm(args, rank, world, local_rank)
         if args.config in ENGINE:
             return run_engine(args, rank, world, local_rank)
         if cfg is None:

@@ -56,6 +56,8 @@ EXPORTED_SYMBOLS = (
     "vmps_embed_rmsnorm",
     "vmps_decode_gemm_supported",
     "vmps_decode_gemm",
+    "vmps_batch_gemm_split",
+    "vmps_batch_gemm",
     "vmps_stage_copy",
     "vmps_debug_error_word",
 )
@@ -112,6 +114,10 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.vmps_decode_gemm_supported.argtypes = [i32, i32, i32, i32]
         lib.vmps_decode_gemm.restype = i32
         lib.vmps_decode_gemm.argtypes = [vp, i64, vp, i64, vp, i32, i32, i32, i32, i32, vp]
+        lib.vmps_batch_gemm_split.restype = i32
+        lib.vmps_batch_gemm_split.argtypes = [i32, i32, i32]
+        lib.vmps_batch_gemm.restype = i32
+        lib.vmps_batch_gemm.argtypes = [vp, i64, vp, i64, vp, i32, i32, i32, i32, vp]
         lib.vmps_stage_copy.restype = i32
         lib.vmps_stage_copy.argtypes = [vp, vp, sz, vp]
         lib.vmps_debug_error_word.restype = i32
@@ -575,6 +581,47 @@ def decode_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = Non
         rc = lib.vmps_decode_gemm(_ptr(out), out.stride(0), _ptr(x), x.stride(0), _ptr(w), M, N, K,
                                   int(bool(silu_mul)), dtype_code(x.dtype), _stream(dev))
     _check(rc, "decode_gemm")
+    return out
+
+
+def batch_gemm_split(m: int, n: int, k: int) -> int:
+    """CTAs per output tile (split-K cluster size) ``batch_gemm`` uses for this
+    shape on the current device, or 0 when the shape is not built
+    (1 <= M <= 256, N % 128 == 0, K % 64 == 0).  Needs a CUDA device."""
+    return int(load_library().vmps_batch_gemm_split(int(m), int(n), int(k)))
+
+
+def batch_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ w.T`` at decode batch sizes up to 256 on the tcgen05 tensor cores.
+
+    ``x``: (M, K) with unit inner stride and rows a multiple of 8 elements
+    apart; ``w``: contiguous (N, K), N % 128 == 0, K % 64 == 0; fp16 or bf16.
+    fp32 accumulation, one rounding (nn.Linear without bias).  Narrow shapes
+    split K over a thread-block cluster (``batch_gemm_split``) and reduce the
+    partials in distributed shared memory.  Returns ``out`` (M, N).
+    """
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be 2-D (M, K) with unit inner stride")
+    if w.dim() != 2 or not w.is_contiguous():
+        raise ValueError("w must be a contiguous (N, K) matrix")
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"x has K={K}, w has K={w.shape[1]}")
+    if w.dtype != x.dtype:
+        raise TypeError(f"w dtype {w.dtype} != x dtype {x.dtype}")
+    if out is None:
+        out = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    elif out.shape != (M, N) or out.dtype != x.dtype or out.stride(1) != 1:
+        raise ValueError(f"out must be ({M}, {N}) of x's dtype with unit inner stride")
+    if M == 0:
+        return out
+    dev = _require_cuda(x, w, out)
+    lib = load_library()
+    with torch.cuda.device(dev):
+        rc = lib.vmps_batch_gemm(_ptr(out), out.stride(0), _ptr(x), x.stride(0), _ptr(w), M, N, K,
+                                 dtype_code(x.dtype), _stream(dev))
+    _check(rc, "batch_gemm")
     return out
 
 
