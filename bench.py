@@ -472,12 +472,20 @@ def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
     # step its early launch) -- then the decode step, then a copy-engine D2H
     # of the step's output on a copy stream.  Every step writes its own
     # device output buffer, so the chain never waits for a D2H.
-    # Step i+1's inputs are staged right BEFORE step i's decode kernel: the
-    # fused step reads its lengths and block tables before its PDL wait, so
-    # the kernel just ahead of it must not be the one writing them (three
-    # staging buffers keep the copy clear of the two steps around it).
+    # Inputs are staged two steps per copy kernel: steps 2p+1 and 2p+2 in one
+    # stage_copy right BEFORE step 2p's decode kernel (one extra link in the
+    # chain per two steps).  The fused step reads its lengths and block tables
+    # before its PDL wait, so the kernel just ahead of it must not be the one
+    # writing them; here every step is at least one decode kernel behind its
+    # copy.  Three pair slots keep a copy clear of the steps around it; the
+    # host side holds each replica's packed inputs followed by the next's, so
+    # a pair is one contiguous source.
     e2e_steps = min(args.steps, 512)
-    stage = [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(3)]
+    stage0 = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    pair_slots = [torch.empty(2 * nbytes, dtype=torch.uint8, device=dev) for _ in range(3)]
+    host_cat = torch.empty((R + 1) * nbytes, dtype=torch.uint8).pin_memory()
+    for r in range(R + 1):
+        host_cat[r * nbytes:(r + 1) * nbytes].copy_(packed[r % R][0])
     douts = [torch.empty((B, n_q, D), dtype=tdt, device=dev) for _ in range(e2e_steps)]
     houts = [torch.empty((B, n_q, D), dtype=tdt).pin_memory() for _ in range(2)]
     maxb_r = tables[0].shape[1]
@@ -490,7 +498,15 @@ def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
                 sl(4).view(torch.int32), sl(5).view(torch.int32),
                 sl(6).view(torch.int32).view(B, maxb_r))
 
-    staged = [views(b) for b in stage]
+    staged0 = views(stage0)
+    staged_pairs = [(views(b[:nbytes]), views(b[nbytes:])) for b in pair_slots]
+
+    def staged_for(i):
+        if i == 0:
+            return staged0
+        p = (i - 1) // 2
+        return staged_pairs[p % 3][(i - 1) % 2]
+
     s_d2h = torch.cuda.Stream(dev)
     k_done = [torch.cuda.Event() for _ in range(2)]
 
@@ -499,13 +515,16 @@ def decode_leg(args, cfg_name, rank, world, local_rank, cpu_base=True):
         if first is not None:
             first.record(comp)
         # The first step's inputs go by copy engine (a full dependency): a
-        # stage copy lets the next launch start at once, so two adjacent
-        # stage copies would not order step 0's inputs before it starts.
-        stage[0].copy_(packed[0][0], non_blocking=True)
+        # stage copy lets the next launch start at once, so a stage copy just
+        # ahead of step 0 would not order step 0's inputs before it starts.
+        stage0.copy_(packed[0][0], non_blocking=True)
         for i in range(n):
-            if i + 1 < n:
-                K.stage_copy(stage[(i + 1) % 3], packed[(i + 1) % R][0])
-            dq, dk, dv, dpos, dsl, dslot, dbt = staged[i % 3]
+            if i % 2 == 0 and i + 1 < n:
+                j = i + 1  # steps j and j + 1 (replicas j % R and j % R + 1 in host_cat)
+                cnt = 2 if j + 1 < n else 1
+                src = host_cat[(j % R) * nbytes:(j % R + cnt) * nbytes]
+                K.stage_copy(pair_slots[((j - 1) // 2) % 3][:cnt * nbytes], src)
+            dq, dk, dv, dpos, dsl, dslot, dbt = staged_for(i)
             K.paged_decode_step(dq, dk, dv, dpos, dslot, inv, pools[i % R], dbt, dsl,
                                 out=douts[i], workspace=ws)
             b = i % 2
