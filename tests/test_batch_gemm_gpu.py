@@ -4,10 +4,11 @@ The kernel accumulates in fp32 and rounds once, like the nn.Linear it
 replaces, so every element is within one 16-bit rounding of the fp32 product
 (the fp32 summation order differs: a few ulps of fp32, which can move a
 rounding by one 16-bit ulp).  Shapes: the Llama-3-8B and TinyLlama
-projections at batch 256 (split-K over 3, 4, 7 and 8 CTAs, and unsplit),
+projections at batch 256 (split-K over 2 to 4 CTAs, and unsplit),
 batches that are not multiples of 16, strided x and out, a single tile.
 Results are bit-identical from run to run (the split partials are summed in
-rank order).
+rank order), and the output tiles are written by TMA stores that clip at M
+and touch nothing outside ``out``.
 """
 
 import pytest
@@ -62,7 +63,7 @@ def test_batch_gemm_splits_the_narrow_shapes(cuda_device):
 
     sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
     split = K_.batch_gemm_split(256, 4096, 4096)
-    assert 2 <= split <= 8 and 32 * split <= sms
+    assert 2 <= split <= 4 and 32 * split <= sms
     assert K_.batch_gemm_split(256, 28672, 4096) == 1  # 224 tiles: no split
     assert K_.batch_gemm_split(256, 4096, 100) == 0    # K % 64
     assert K_.batch_gemm_split(257, 4096, 4096) == 0   # M > 256
