@@ -267,13 +267,15 @@ int vmps_decode_gemm(void* out, int64_t out_row_stride, const void* x, int64_t x
  * nn.Linear calls of models/llama_adapter.py:137-207 at the engine's batch;
  * no kernel counterpart in the reference): out[M, N] = x[M, K] . w[N, K]^T,
  * fp16 or bf16, fp32 accumulation on the tcgen05 tensor cores, one rounding.
- * Requires N % 128 == 0, K % 64 == 0, x and w 16-byte aligned, x rows a
- * multiple of 8 elements apart, out rows at least N elements apart.  Narrow
- * shapes split K over a thread-block cluster of up to 8 CTAs whose fp32
- * partials are summed (in a fixed order) in distributed shared memory;
- * vmps_batch_gemm_split returns that cluster size for a shape on the current
- * device (0 = shape not built).  Launched with programmatic dependent
- * launch: the weight stream starts before the previous kernel has finished.
+ * Requires N % 128 == 0, K % 64 == 0, x, w and out 16-byte aligned, x and
+ * out rows a multiple of 8 elements apart (x rows at least K, out rows at
+ * least N).  Narrow shapes split K over a thread-block cluster of up to 4
+ * CTAs whose fp32 partials are summed (in a fixed order) through a scratch
+ * area inside the library, so calls must not overlap on the GPU (calls on
+ * one stream never do); vmps_batch_gemm_split returns that cluster size for
+ * a shape on the current device (0 = shape not built).  Launched with
+ * programmatic dependent launch: the weight stream starts before the
+ * previous kernel has finished.
  */
 int vmps_batch_gemm_split(int M, int N, int K);
 int vmps_batch_gemm(void* out, int64_t out_row_stride, const void* x, int64_t x_row_stride,

@@ -595,10 +595,13 @@ def batch_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None
     """``x @ w.T`` at decode batch sizes up to 256 on the tcgen05 tensor cores.
 
     ``x``: (M, K) with unit inner stride and rows a multiple of 8 elements
-    apart; ``w``: contiguous (N, K), N % 128 == 0, K % 64 == 0; fp16 or bf16.
-    fp32 accumulation, one rounding (nn.Linear without bias).  Narrow shapes
-    split K over a thread-block cluster (``batch_gemm_split``) and reduce the
-    partials in distributed shared memory.  Returns ``out`` (M, N).
+    apart; ``w``: contiguous (N, K), N % 128 == 0, K % 64 == 0; fp16 or bf16;
+    ``out`` rows a multiple of 8 elements apart.  fp32 accumulation, one
+    rounding (nn.Linear without bias).  Narrow shapes split K over a
+    thread-block cluster (``batch_gemm_split``) whose partials meet in a
+    scratch area of the library: calls must not overlap on the GPU.  Measured
+    slower than cuBLAS at the engine's shapes; the engine does not call it.
+    Returns ``out`` (M, N).
     """
     if x.dim() != 2 or x.stride(1) != 1:
         raise ValueError("x must be 2-D (M, K) with unit inner stride")
