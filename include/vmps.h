@@ -9,8 +9,10 @@
  *
  * Conventions shared by every entry point:
  *   - All pointers are device pointers unless stated; the caller owns every
- *     buffer (the library allocates nothing and keeps no per-call state
- *     except the device error word).
+ *     buffer.  The library allocates nothing; besides the device error word
+ *     it keeps two fixed scratch arrays in its own device memory, used by
+ *     vmps_paged_decode_attention_noalloc and vmps_batch_gemm (calls of each
+ *     must not overlap on the GPU).
  *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Work is
  *     only enqueued; calls return before the GPU finishes.
  *   - `dtype` is VMPS_DTYPE_F16 or VMPS_DTYPE_BF16 for every 16-bit tensor
