@@ -99,7 +99,9 @@ class ShardedEngine:
         if int(gather_every) < 1:
             raise ValueError("gather_every must be >= 1")
         self.gather_every = int(gather_every)
-        self._pending: list[tuple[int, int, int]] = []
+        # (global request id, token, finished) rows of the local steps since
+        # the last gather, one int32 array per step.
+        self._pending: list[np.ndarray] = []
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -176,8 +178,11 @@ class ShardedEngine:
         if len(produced) > self.capacity:
             raise RuntimeError(f"rank {self.rank}: {len(produced)} sequences in one step "
                                f"exceed the record capacity {self.capacity}")
-        self._pending.extend((self._local_to_global[o.request_id], o.token_ids[-1],
-                              int(o.finished)) for o in produced)
+        if produced:
+            g2l = self._local_to_global
+            self._pending.append(np.array(
+                [(g2l[o.request_id], o.token_ids[-1], o.finished) for o in produced],
+                dtype=np.int32))
         self.steps += 1
         if not force_gather and self.steps % self.gather_every:
             return True
@@ -201,9 +206,9 @@ class ShardedEngine:
         rec = self._send_host[j].numpy()
         rec[:] = -1
         rec[0] = 0 if self.engine.is_finished() else 1
-        n = len(self._pending)
-        if n:
-            rec[1:1 + 3 * n] = np.asarray(self._pending, dtype=np.int32).reshape(-1)
+        if self._pending:
+            rows = np.concatenate(self._pending)
+            rec[1:1 + rows.size] = rows.reshape(-1)
         self._pending.clear()
         send, recv = self._send[j], self._recv[j]
         if self._side is None:  # host tensors (gloo)
@@ -236,12 +241,23 @@ class ShardedEngine:
             body = allrec[r, 1:1 + 3 * slots].reshape(slots, 3)
             neg = np.flatnonzero(body[:, 0] < 0)
             n_r = int(neg[0]) if neg.size else slots
-            for gid, tok, fin in body[:n_r].tolist():
+            if n_r == 0:
+                continue
+            body = body[:n_r]
+            # Group the rows by request, keeping step order within a request
+            # (a stable sort), so the Python loop runs per request, not per token.
+            order = np.argsort(body[:, 0], kind="stable")
+            gids = body[order, 0]
+            starts = np.flatnonzero(np.r_[True, gids[1:] != gids[:-1]])
+            ends = np.r_[starts[1:], n_r]
+            toks = body[order, 1].tolist()
+            fins = body[order, 2]
+            for a, b, gid in zip(starts.tolist(), ends.tolist(), gids[starts].tolist()):
                 o = self.outputs[gid]
                 if o.rank != r:
                     raise RuntimeError(f"request {gid} reported by rank {r}, owned by {o.rank}")
-                o.token_ids.append(tok)
-                o.finished = bool(fin)
+                o.token_ids.extend(toks[a:b])
+                o.finished = bool(fins[b - 1])
         return more
 
     def run(self, max_steps: int | None = None) -> dict[int, ShardedOutput]:
