@@ -790,16 +790,27 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
         __syncwarp();
       }
 
-      // S^T = K . Q^T
-      float sc[NT][4];
+      // S^T = K . Q^T, the K steps in two independent accumulator chains
+      // (even and odd steps) so the MMAs of one page do not wait on each other.
+      float sc[NT][4], sc_odd[NT][4];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      for (int nt = 0; nt < NT; ++nt) {
+        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+        sc_odd[nt][0] = sc_odd[nt][1] = sc_odd[nt][2] = sc_odd[nt][3] = 0.f;
+      }
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
         uint32_t a[4];
         ldmatrix_x4(a, sbase + (ks >> 2) * Shape::kTileBytes + k_off[ks & 3]);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) Mma<T>::run(sc[nt], a, qf[nt][ks][0], qf[nt][ks][1]);
+        for (int nt = 0; nt < NT; ++nt) {
+          Mma<T>::run((ks & 1) ? sc_odd[nt] : sc[nt], a, qf[nt][ks][0], qf[nt][ks][1]);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[nt][e] += sc_odd[nt][e];
       }
 
       // Mask, scale into log2 units, online softmax per head.
@@ -813,26 +824,35 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams
         const float x2 = v1 ? sc[nt][2] * p.scale_log2 : -INFINITY;
         const float x3 = v1 ? sc[nt][3] * p.scale_log2 : -INFINITY;
         float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+        // The running max only has to bound the scores: it is raised (a
+        // reduction over the row groups, and O and l rescaled) only when a
+        // score of this page exceeds it by more than 2^8, so P <= 256 (exact
+        // scaling in the 16-bit P and cancelled by l).  Most pages skip the
+        // shuffles, the exponentials of alpha and the rescale.
+        if (__any_sync(0xffffffffu, mx0 > m_run[nt][0] + 8.f || mx1 > m_run[nt][1] + 8.f)) {
 #pragma unroll
-        for (int sh = 4; sh < 32; sh <<= 1) {
-          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sh));
-          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, sh));
-        }
-        const float mn0 = fmaxf(m_run[nt][0], mx0), mn1 = fmaxf(m_run[nt][1], mx1);
-        const float al0 = fast_exp2(m_run[nt][0] - mn0), al1 = fast_exp2(m_run[nt][1] - mn1);
-        m_run[nt][0] = mn0;
-        m_run[nt][1] = mn1;
-        const float p0 = fast_exp2(x0 - mn0), p1 = fast_exp2(x1 - mn1);
-        const float p2 = fast_exp2(x2 - mn0), p3 = fast_exp2(x3 - mn1);
-        l_run[nt][0] = l_run[nt][0] * al0 + (p0 + p2);
-        l_run[nt][1] = l_run[nt][1] * al1 + (p1 + p3);
+          for (int sh = 4; sh < 32; sh <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sh));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, sh));
+          }
+          const float mn0 = fmaxf(m_run[nt][0], mx0), mn1 = fmaxf(m_run[nt][1], mx1);
+          const float al0 = fast_exp2(m_run[nt][0] - mn0), al1 = fast_exp2(m_run[nt][1] - mn1);
+          m_run[nt][0] = mn0;
+          m_run[nt][1] = mn1;
+          l_run[nt][0] *= al0;
+          l_run[nt][1] *= al1;
 #pragma unroll
-        for (int mt = 0; mt < KS; ++mt) {
-          o[nt][mt][0] *= al0;
-          o[nt][mt][1] *= al1;
-          o[nt][mt][2] *= al0;
-          o[nt][mt][3] *= al1;
+          for (int mt = 0; mt < KS; ++mt) {
+            o[nt][mt][0] *= al0;
+            o[nt][mt][1] *= al1;
+            o[nt][mt][2] *= al0;
+            o[nt][mt][3] *= al1;
+          }
         }
+        const float p0 = fast_exp2(x0 - m_run[nt][0]), p1 = fast_exp2(x1 - m_run[nt][1]);
+        const float p2 = fast_exp2(x2 - m_run[nt][0]), p3 = fast_exp2(x3 - m_run[nt][1]);
+        l_run[nt][0] += p0 + p2;
+        l_run[nt][1] += p1 + p3;
         // C fragment (row = token, col = head) -> B fragment (k = token, n = head).
         pb[nt][0] = movmatrix_trans(Elt<T>::pack(p0, p1));
         pb[nt][1] = movmatrix_trans(Elt<T>::pack(p2, p3));
