@@ -176,6 +176,34 @@ __device__ __forceinline__ uint32_t f16_idesc(int n, bool b_mn_major) {
 
 __device__ __forceinline__ bool aborted(volatile int* flag) { return *flag != 0; }
 
+// ── packed fp32 pairs (f32x2 arithmetic of sm_100) for the softmax ───────────
+// Each op computes two independent fp32 results, rounded exactly as the
+// scalar op would, in one instruction.
+
+__device__ __forceinline__ uint64_t f2_make(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kPfThreads, 2)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap kv_map,
@@ -422,7 +450,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       // keys (position > row) become -inf; the warp takes the masked path
       // together whenever any of its rows needs it.
       const bool needs_mask = __any_sync(0xffffffffu, key0 + KEYS - 1 > row_pos);
-      // Four independent partial maxima (short dependency chains).
+      // Four independent partial maxima (short dependency chains), two
+      // scores per three-input max.
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if (needs_mask) {
 #pragma unroll
@@ -430,14 +459,15 @@ __global__ void __launch_bounds__(kPfThreads, 2)
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             if (key0 + c * 16 + i > row_pos) s[c][i] = __float_as_uint(-INFINITY);
-            mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(s[c][i]));
           }
         }
-      } else {
+      }
 #pragma unroll
-        for (int c = 0; c < KEYS / 16; ++c) {
+      for (int c = 0; c < KEYS / 16; ++c) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(s[c][i]));
+        for (int i = 0; i < 8; ++i) {
+          mx4[i & 3] = fmax3(mx4[i & 3], __uint_as_float(s[c][2 * i]),
+                             __uint_as_float(s[c][2 * i + 1]));
         }
       }
       float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
@@ -470,20 +500,29 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       // P = exp2(s - m_run) as 16-bit pairs over the first KEYS/2 columns of
       // this S buffer (A operand of PV(j) in TMEM: row = lane, key pairs per
       // 32-bit column).
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent partial sums
+      // The scale-and-subtract and the row sum run as packed pairs.
       uint32_t pk[KEYS / 32][16];
+      uint64_t acc2[2] = {0ull, 0ull};  // two independent packed partial sums
+      const uint64_t scale2 = f2_make(p.scale_log2, p.scale_log2);
+      const uint64_t neg_m2 = f2_make(-m_run, -m_run);
 #pragma unroll
       for (int c = 0; c < KEYS / 16; ++c) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float a = fast_exp2(fmaf(__uint_as_float(s[c][2 * i]), p.scale_log2, -m_run));
-          const float b =
-              fast_exp2(fmaf(__uint_as_float(s[c][2 * i + 1]), p.scale_log2, -m_run));
-          sum4[i & 3] += a + b;
+          float a, b;
+          f2_split(f2_fma(f2_make(__uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1])),
+                          scale2, neg_m2),
+                   a, b);
+          a = fast_exp2(a);
+          b = fast_exp2(b);
+          acc2[i & 1] = f2_add(acc2[i & 1], f2_make(a, b));
           pk[c >> 1][(c & 1) * 8 + i] = Elt<T>::pack(a, b);
         }
       }
-      const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+      float s0, s1, s2, s3;
+      f2_split(acc2[0], s0, s1);
+      f2_split(acc2[1], s2, s3);
+      const float sum = (s0 + s1) + (s2 + s3);
 #pragma unroll
       for (int c = 0; c < KEYS / 32; ++c) tmem_st16(t_s + c * 16, pk[c]);
       tmem_st_wait();
