@@ -301,3 +301,28 @@ def test_model_config_from_a_local_checkpoint_directory(tmp_path):
     cfg = ModelConfig.from_pretrained(str(tmp_path))
     assert (cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.d_k, cfg.n_layers) == (256, 8, 2, 32, 3)
     assert cfg.architecture == "llama" and cfg.rope_theta == 250000.0 and cfg.max_seq_len == 4096
+
+
+def test_bench_tensor_peak_matches_the_timed_region(tmp_path, monkeypatch):
+    """bench.py's tensor roofline uses the measured burst bf16 peak for a
+    short timed region and the measured sustained one for a region of half a
+    second or more (which runs under the power cap like the sustained loop),
+    and reports the other figure beside it."""
+    import json
+    import os
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+
+    (tmp_path / "MEASURED_PEAKS.json").write_text(
+        json.dumps({"bf16_tflops": 1600.0, "bf16_tflops_sustained": 1400.0}))
+    monkeypatch.setattr(bench, "ROOT", str(tmp_path))
+    peak, kind, other = bench.tensor_peak(0.05)
+    assert peak == 1600.0 and kind.startswith("measured (burst") and other == (1400.0, "sustained")
+    peak, kind, other = bench.tensor_peak(bench.SUSTAINED_AFTER_S)
+    assert peak == 1400.0 and kind.startswith("measured (sustained") and other == (1600.0, "burst")
+    (tmp_path / "MEASURED_PEAKS.json").write_text(json.dumps({"bf16_tflops": 1600.0}))
+    assert bench.tensor_peak(2.0)[:2] == (1600.0, "measured (burst: 2.000 s timed)")
+    (tmp_path / "MEASURED_PEAKS.json").unlink()
+    assert bench.tensor_peak(2.0) == (1590.0, "fallback", None)
