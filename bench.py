@@ -1336,9 +1336,14 @@ def run_bgemm(args, rank, world, local_rank):
         torch.cuda.synchronize(dev)
         return e0.elapsed_time(e1) * 1e-3
 
+    # One split-K workspace per projection, allocated before any capture.
+    WS = {n: torch.empty(max(16, K.batch_gemm_workspace_bytes(M, N, Kd, X[n].dtype)),
+                         dtype=torch.uint8, device=dev)
+          for n, M, N, Kd in BGEMM_SHAPES}
+
     def step(r):
         for n, *_ in BGEMM_SHAPES:
-            K.batch_gemm(X[n], W[n][r], out=OUT[n])
+            K.batch_gemm(X[n], W[n][r], out=OUT[n], workspace=WS[n])
 
     g_steps = capture([lambda r=r: step(r) for r in range(R)])
     for _ in range(max(1, args.warmup // R)):
@@ -1354,7 +1359,7 @@ def run_bgemm(args, rank, world, local_rank):
 
         def ours(n=n):
             it[0] = (it[0] + 1) % R
-            K.batch_gemm(X[n], W[n][it[0]], out=OUT[n])
+            K.batch_gemm(X[n], W[n][it[0]], out=OUT[n], workspace=WS[n])
 
         def cublas(n=n):
             it[0] = (it[0] + 1) % R

@@ -10,9 +10,9 @@
  * Conventions shared by every entry point:
  *   - All pointers are device pointers unless stated; the caller owns every
  *     buffer.  The library allocates nothing; besides the device error word
- *     it keeps two fixed scratch arrays in its own device memory, used by
- *     vmps_paged_decode_attention_noalloc and vmps_batch_gemm (calls of each
- *     must not overlap on the GPU).
+ *     it keeps one fixed scratch array in its own device memory, used only
+ *     by vmps_paged_decode_attention_noalloc (its calls must not overlap on
+ *     the GPU).
  *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Work is
  *     only enqueued; calls return before the GPU finishes.
  *   - `dtype` is VMPS_DTYPE_F16 or VMPS_DTYPE_BF16 for every 16-bit tensor
@@ -272,16 +272,21 @@ int vmps_decode_gemm(void* out, int64_t out_row_stride, const void* x, int64_t x
  * Requires N % 128 == 0, K % 64 == 0, x, w and out 16-byte aligned, x and
  * out rows a multiple of 8 elements apart (x rows at least K, out rows at
  * least N).  Narrow shapes split K over a thread-block cluster of up to 4
- * CTAs whose fp32 partials are summed (in a fixed order) through a scratch
- * area inside the library, so calls must not overlap on the GPU (calls on
- * one stream never do); vmps_batch_gemm_split returns that cluster size for
- * a shape on the current device (0 = shape not built).  Launched with
- * programmatic dependent launch: the weight stream starts before the
- * previous kernel has finished.
+ * CTAs whose fp32 partials are summed (in a fixed order) through the
+ * caller's workspace: vmps_batch_gemm_split returns that cluster size for a
+ * shape on the current device (0 = shape not built) and
+ * vmps_batch_gemm_workspace_bytes the workspace it needs (0 = none; at most
+ * 16 MiB), which must be 16-byte aligned; it needs no initialisation, and
+ * calls that may overlap on the GPU need different workspaces (calls on one
+ * stream never overlap).  VMPS_ERR_WORKSPACE if it is missing or too small.
+ * Launched with programmatic dependent launch: the weight stream starts
+ * before the previous kernel has finished.
  */
 int vmps_batch_gemm_split(int M, int N, int K);
+size_t vmps_batch_gemm_workspace_bytes(int M, int N, int K, int dtype);
 int vmps_batch_gemm(void* out, int64_t out_row_stride, const void* x, int64_t x_row_stride,
-                    const void* w, int M, int N, int K, int dtype, void* stream);
+                    const void* w, int M, int N, int K, void* workspace, size_t workspace_bytes,
+                    int dtype, void* stream);
 
 /*
  * Copies `bytes` from `src` to `dst` with the GPU's own loads and stores,

@@ -7,8 +7,8 @@ rounding by one 16-bit ulp).  Shapes: the Llama-3-8B and TinyLlama
 projections at batch 256 (split-K over 2 to 4 CTAs, and unsplit),
 batches that are not multiples of 16, strided x and out, a single tile.
 Results are bit-identical from run to run (the split partials are summed in
-rank order), and the output tiles are written by TMA stores that clip at M
-and touch nothing outside ``out``.
+rank order, through the caller's workspace), and the output tiles are
+written by TMA stores that clip at M and touch nothing outside ``out``.
 """
 
 import pytest
@@ -68,6 +68,45 @@ def test_batch_gemm_splits_the_narrow_shapes(cuda_device):
     assert K_.batch_gemm_split(256, 4096, 100) == 0    # K % 64
     assert K_.batch_gemm_split(257, 4096, 4096) == 0   # M > 256
     assert K_.batch_gemm_split(8, 4000, 4096) == 0     # N % 128
+    # The split-K partials go through the caller's workspace: needed exactly
+    # when K is split.
+    assert K_.batch_gemm_workspace_bytes(256, 4096, 4096, torch.bfloat16) > 0
+    assert K_.batch_gemm_workspace_bytes(256, 28672, 4096, torch.bfloat16) == 0
+    assert K_.batch_gemm_workspace_bytes(256, 4096, 100, torch.bfloat16) == 0  # not built
+
+
+def test_batch_gemm_workspace_contract(cuda_device):
+    """A split shape with a missing or too-small workspace is rejected on the
+    host (VMPS_ERR_WORKSPACE, nothing launched); a caller's own workspace,
+    reused across calls, gives the same bits as a fresh one."""
+    import ctypes
+
+    from vllm_mps_b200 import kernels as K_
+
+    M, N, K = 256, 4096, 4096
+    need = K_.batch_gemm_workspace_bytes(M, N, K, torch.bfloat16)
+    assert need > 0 and K_.batch_gemm_split(M, N, K) > 1
+    g = torch.Generator(device=cuda_device).manual_seed(9)
+    x = (torch.randn(M, K, generator=g, device=cuda_device) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g, device=cuda_device) / K ** 0.5).to(torch.bfloat16)
+    lib = K_.load_library()
+    out = torch.zeros(M, N, device=cuda_device, dtype=torch.bfloat16)
+    small = torch.empty(need - 16, dtype=torch.uint8, device=cuda_device)
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    for ws, nbytes in ((None, 0), (small, need - 16)):
+        rc = lib.vmps_batch_gemm(out.data_ptr(), N, x.data_ptr(), K, w.data_ptr(), M, N, K,
+                                 None if ws is None else ws.data_ptr(), nbytes, 1, stream)
+        assert rc == -4, rc
+        assert b"workspace" in lib.vmps_last_error()
+    torch.cuda.synchronize(cuda_device)
+    assert torch.count_nonzero(out) == 0
+    ws = torch.empty(need, dtype=torch.uint8, device=cuda_device)
+    a = K_.batch_gemm(x, w, workspace=ws)
+    b = K_.batch_gemm(x, w, workspace=ws)
+    c = K_.batch_gemm(x, w)
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    assert torch.equal(a.view(torch.int16), c.view(torch.int16))
+    _check(a, x, w)
 
 
 def test_batch_gemm_strided_operands(cuda_device):

@@ -26,8 +26,8 @@
 //  * Split-K over a thread-block cluster of S <= 4 CTAs (same tile, K split
 //    in S ranges), S chosen so the whole grid is resident at once
 //    (cudaOccupancyMaxActiveClusters).  Each CTA owns 1/S of the batch
-//    columns; the others store their fp32 partials of those columns to an
-//    L2-resident scratch area (coalesced 16-byte stores), one cluster
+//    columns; the others store their fp32 partials of those columns to the
+//    caller's workspace, which stays in L2 (coalesced 16-byte stores), one cluster
 //    barrier orders them, and the owner adds them to its own accumulator in
 //    rank order (deterministic) before rounding.
 //  * Warps 3-6 are the epilogue, one thread per output feature (TMEM lane):
@@ -37,8 +37,8 @@
 //
 // Every mbarrier wait is bounded (kDevErrTimeout and an abort flag on expiry);
 // an aborting CTA still takes the cluster barrier, waits (bounded) for its
-// own TMA loads in flight and frees its TMEM.  Calls must not overlap on the
-// GPU (they share the scratch area); a stream's calls never do.
+// own TMA loads in flight and frees its TMEM.  Calls that may overlap on the
+// GPU need different workspaces; a stream's calls never overlap.
 #include <type_traits>
 #include <mutex>
 
@@ -58,9 +58,9 @@ constexpr int kBgBarBytes = 256;
 constexpr int kBgMaxSplit = 4;
 constexpr int kBgMaxM = 256;     // MMA N limit
 constexpr int kBgOutTile = 16 * kBgRows * 2;  // one 16-row output tile (16-bit)
-// Split-K scratch: [tile][owner][sender][group][row][16] fp32.
+// Split-K workspace: [tile][owner][sender][group][row][16] fp32.  The split
+// is chosen so that it needs at most this much.
 constexpr size_t kBgScratchFloats = (16u << 20) / 4;
-__device__ float g_bg_scratch[kBgScratchFloats];
 
 struct BgParams {
   void* out;
@@ -71,6 +71,7 @@ struct BgParams {
   int groups;  // Mp / 16 column groups
   int maxg;    // most groups one CTA owns
   uint32_t tmem_cols;
+  float* scratch;  // the caller's workspace (split > 1)
   int* err;
 };
 
@@ -277,7 +278,7 @@ __global__ void __launch_bounds__(kBgThreads, 1)
   const int G = p.groups;
   // Scratch slot of (owner d, sender slot q, owner-local group gi): 128 rows x 16.
   auto slot = [&](int d, int q, int gi) {
-    return g_bg_scratch +
+    return p.scratch +
            ((((static_cast<size_t>(tile) * S + d) * (S - 1) + q) * p.maxg + gi) * kBgRows + row) * 16;
   };
   if (S > 1) {
@@ -365,6 +366,7 @@ struct BgPlan {
   int Mp, groups, split, wstages, xstages, maxg;
   uint32_t tmem_cols;
   size_t smem;
+  size_t scratch_bytes;  // split-K partials: the workspace a call needs
 };
 
 size_t bg_smem_bytes(int wstages, int xstages, int Mp) {
@@ -422,7 +424,7 @@ int bg_max_clusters(int split, int Mp, size_t smem) {
 // Rings: x in 2-4 stages of Mp x 128 B, W in as many 16 KB stages as fit (up
 // to 8).  Split: the largest S <= 4 (each CTA keeping at least four K chunks)
 // whose grid of clusters fits on the device at once and whose partials fit
-// the scratch area; otherwise none.
+// in kBgScratchFloats; otherwise none.
 template <typename T>
 bool bg_plan(int M, int N, int K, BgPlan* pl) {
   if (M < 1 || M > kBgMaxM || N < kBgRows || N % kBgRows || K < 64 || K % 64) return false;
@@ -457,6 +459,9 @@ bool bg_plan(int M, int N, int K, BgPlan* pl) {
   pl->maxg = (groups + split - 1) / split;
   pl->tmem_cols = cols;
   pl->smem = smem;
+  pl->scratch_bytes = split > 1 ? static_cast<size_t>(tiles) * split * (split - 1) * pl->maxg *
+                                      kBgRows * 16 * sizeof(float)
+                                : 0;
   return true;
 }
 
@@ -496,9 +501,16 @@ extern "C" int vmps_batch_gemm_split(int M, int N, int K) {
   return bg_plan<__nv_bfloat16>(M, N, K, &pl) ? pl.split : 0;
 }
 
+extern "C" size_t vmps_batch_gemm_workspace_bytes(int M, int N, int K, int dtype) {
+  BgPlan pl;
+  if (dtype == VMPS_DTYPE_F16) return bg_plan<__half>(M, N, K, &pl) ? pl.scratch_bytes : 0;
+  if (dtype == VMPS_DTYPE_BF16) return bg_plan<__nv_bfloat16>(M, N, K, &pl) ? pl.scratch_bytes : 0;
+  return 0;
+}
+
 extern "C" int vmps_batch_gemm(void* out, int64_t out_row_stride, const void* x,
-                               int64_t x_row_stride, const void* w, int M, int N, int K, int dtype,
-                               void* stream) {
+                               int64_t x_row_stride, const void* w, int M, int N, int K,
+                               void* workspace, size_t workspace_bytes, int dtype, void* stream) {
   clear_error();
   if (dtype != VMPS_DTYPE_F16 && dtype != VMPS_DTYPE_BF16) {
     return fail(VMPS_ERR_INVALID_ARG, "batch_gemm: dtype %d", dtype);
@@ -510,6 +522,13 @@ extern "C" int vmps_batch_gemm(void* out, int64_t out_row_stride, const void* x,
     return fail(VMPS_ERR_UNSUPPORTED,
                 "batch_gemm: M=%d N=%d K=%d (1 <= M <= %d, N %% 128 == 0, K %% 64 == 0)", M, N, K,
                 kBgMaxM);
+  }
+  if (pl.scratch_bytes > 0 && (!workspace || workspace_bytes < pl.scratch_bytes ||
+                               !aligned16(workspace))) {
+    return fail(VMPS_ERR_WORKSPACE,
+                "batch_gemm: this shape splits K over %d CTAs and needs a 16-byte aligned "
+                "workspace of %zu bytes (got %zu; see vmps_batch_gemm_workspace_bytes)",
+                pl.split, pl.scratch_bytes, workspace ? workspace_bytes : size_t(0));
   }
   if (!out || !x || !w) return fail(VMPS_ERR_INVALID_ARG, "batch_gemm: NULL pointer");
   if (!aligned16(x) || !aligned16(w) || !aligned16(out) || (x_row_stride % 8) || x_row_stride < K ||
@@ -566,6 +585,7 @@ extern "C" int vmps_batch_gemm(void* out, int64_t out_row_stride, const void* x,
   p.groups = pl.groups;
   p.maxg = pl.maxg;
   p.tmem_cols = pl.tmem_cols;
+  p.scratch = static_cast<float*>(workspace);
   p.err = err;
   const dim3 grid(pl.split, N / kBgRows);
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -57,6 +57,7 @@ EXPORTED_SYMBOLS = (
     "vmps_decode_gemm_supported",
     "vmps_decode_gemm",
     "vmps_batch_gemm_split",
+    "vmps_batch_gemm_workspace_bytes",
     "vmps_batch_gemm",
     "vmps_stage_copy",
     "vmps_debug_error_word",
@@ -116,8 +117,11 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.vmps_decode_gemm.argtypes = [vp, i64, vp, i64, vp, i32, i32, i32, i32, i32, vp]
         lib.vmps_batch_gemm_split.restype = i32
         lib.vmps_batch_gemm_split.argtypes = [i32, i32, i32]
+        lib.vmps_batch_gemm_workspace_bytes.restype = ctypes.c_size_t
+        lib.vmps_batch_gemm_workspace_bytes.argtypes = [i32, i32, i32, i32]
         lib.vmps_batch_gemm.restype = i32
-        lib.vmps_batch_gemm.argtypes = [vp, i64, vp, i64, vp, i32, i32, i32, i32, vp]
+        lib.vmps_batch_gemm.argtypes = [vp, i64, vp, i64, vp, i32, i32, i32, vp, ctypes.c_size_t,
+                                        i32, vp]
         lib.vmps_stage_copy.restype = i32
         lib.vmps_stage_copy.argtypes = [vp, vp, sz, vp]
         lib.vmps_debug_error_word.restype = i32
@@ -591,17 +595,26 @@ def batch_gemm_split(m: int, n: int, k: int) -> int:
     return int(load_library().vmps_batch_gemm_split(int(m), int(n), int(k)))
 
 
-def batch_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def batch_gemm_workspace_bytes(m: int, n: int, k: int, dtype: torch.dtype) -> int:
+    """Bytes of workspace ``batch_gemm`` needs for this shape (0: none, or not built)."""
+    return int(load_library().vmps_batch_gemm_workspace_bytes(int(m), int(n), int(k),
+                                                              dtype_code(dtype)))
+
+
+def batch_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
+               workspace: torch.Tensor | None = None) -> torch.Tensor:
     """``x @ w.T`` at decode batch sizes up to 256 on the tcgen05 tensor cores.
 
     ``x``: (M, K) with unit inner stride and rows a multiple of 8 elements
     apart; ``w``: contiguous (N, K), N % 128 == 0, K % 64 == 0; fp16 or bf16;
     ``out`` rows a multiple of 8 elements apart.  fp32 accumulation, one
     rounding (nn.Linear without bias).  Narrow shapes split K over a
-    thread-block cluster (``batch_gemm_split``) whose partials meet in a
-    scratch area of the library: calls must not overlap on the GPU.  Measured
-    slower than cuBLAS at the engine's shapes; the engine does not call it.
-    Returns ``out`` (M, N).
+    thread-block cluster (``batch_gemm_split``) whose fp32 partials meet in
+    a workspace of ``batch_gemm_workspace_bytes`` bytes: ``workspace`` (a
+    device tensor of at least that many bytes), else one from torch's caching
+    allocator for this call (stream-ordered, so calls on different streams
+    never share it).  Measured slower than cuBLAS at the engine's shapes; the
+    engine does not call it.  Returns ``out`` (M, N).
     """
     if x.dim() != 2 or x.stride(1) != 1:
         raise ValueError("x must be 2-D (M, K) with unit inner stride")
@@ -622,8 +635,12 @@ def batch_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None
     dev = _require_cuda(x, w, out)
     lib = load_library()
     with torch.cuda.device(dev):
+        need = int(lib.vmps_batch_gemm_workspace_bytes(M, N, K, dtype_code(x.dtype)))
+        if workspace is None and need > 0:
+            workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+        ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
         rc = lib.vmps_batch_gemm(_ptr(out), out.stride(0), _ptr(x), x.stride(0), _ptr(w), M, N, K,
-                                 dtype_code(x.dtype), _stream(dev))
+                                 _ptr(workspace), ws_bytes, dtype_code(x.dtype), _stream(dev))
     _check(rc, "batch_gemm")
     return out
 
