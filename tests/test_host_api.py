@@ -58,6 +58,16 @@ def test_host_side_argument_checks_need_no_gpu():
     rc = lib.vmps_paged_decode_attention(None, None, None, None, 1, None, 0, 8, 2, 64, 16, 10,
                                          0.1, None, 0, 0, None)
     assert rc == 0  # empty batch: nothing to do
+    # Misaligned pointers are refused on the host (the kernels are never
+    # given an address their 16-byte loads or 16-bit stores cannot use).
+    # The pointers are never dereferenced on this path.
+    base = 1 << 20
+    rc = lib.vmps_paged_decode_attention(base, base + 8, base, base, 1, base, 4, 8, 2, 64, 16, 10,
+                                         0.1, None, 0, 0, None)
+    assert rc == -3 and b"aligned" in lib.vmps_last_error()  # q not 16-byte aligned
+    rc = lib.vmps_paged_decode_attention(base + 1, base, base, base, 1, base, 4, 8, 2, 64, 16, 10,
+                                         0.1, None, 0, 0, None)
+    assert rc == -3 and b"out must be 2-byte aligned" in lib.vmps_last_error()
     # Decode GEMM: shapes outside what is built are refused before any CUDA call.
     assert lib.vmps_decode_gemm_supported(8, 2560, 2048, 0) == 1
     assert lib.vmps_decode_gemm_supported(9, 2560, 2048, 0) == 0   # M <= 8

@@ -1168,6 +1168,9 @@ static int decode_enqueue(void* out, const void* q, int64_t q_stride, const void
                 "elements",
                 what);
   }
+  if (reinterpret_cast<uintptr_t>(out) & 1) {  // 16-bit element stores
+    return fail(VMPS_ERR_ALIGNMENT, "%s: out must be 2-byte aligned", what);
+  }
   if (q_stride < static_cast<int64_t>(n_q) * head_dim ||
       (fused && (k_stride < static_cast<int64_t>(n_kv) * head_dim ||
                  v_stride < static_cast<int64_t>(n_kv) * head_dim))) {
