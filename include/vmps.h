@@ -113,7 +113,8 @@ int vmps_paged_decode_workspace_init(void* workspace, size_t workspace_bytes, vo
  * t % block_size of block block_tables[i * max_blocks_per_seq + t / block_size].
  * Computed with fp32 scores, fp32 online softmax and fp32 accumulation;
  * out is rounded once to the model dtype.  q and out are [num_seqs][n_q][head_dim]
- * contiguous; seq_lens counts the new token; block tables are int32, only
+ * contiguous (q and the pool 16-byte aligned, out 2-byte aligned:
+ * VMPS_ERR_ALIGNMENT otherwise); seq_lens counts the new token; block tables are int32, only
  * the first ceil(seq_len / block_size) entries of a row are read.  A
  * sequence with seq_len 0 gets a zero output row.
  *
