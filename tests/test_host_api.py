@@ -336,3 +336,27 @@ def test_bench_tensor_peak_matches_the_timed_region(tmp_path, monkeypatch):
     assert bench.tensor_peak(2.0)[:2] == (1600.0, "measured (burst: 2.000 s timed)")
     (tmp_path / "MEASURED_PEAKS.json").unlink()
     assert bench.tensor_peak(2.0) == (1590.0, "fallback", None)
+
+
+def test_bench_algorithmic_bytes_of_config_1():
+    """The roofline numerator bench.py reports for config 1, recomputed from
+    its definition on the bench's seeded workload (rank 0): every context's
+    K and V rows of all kv heads, q in and out, the block-table entries read
+    and the lengths; the fused step adds the new token's k and v read, its
+    rotated K and V written, and positions and slots read."""
+    import os
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+
+    cfg = bench.CONFIGS["c1"]
+    B, n_q, n_kv, D = cfg[0], cfg[1], cfg[2], cfg[3]
+    ctx, pages, _ = bench.make_host_workload(cfg, seed=1000)
+    assert int(ctx.sum()) == 65186 and (pages == (ctx + 15) // 16).all()
+    e = 2
+    attn = (int(ctx.sum()) * n_kv * D * 2 * e + 2 * B * n_q * D * e
+            + int(pages.sum()) * 4 + 4 * B)
+    fused = attn + 2 * B * n_kv * D * e * 2 + 2 * 4 * B
+    assert bench.alg_bytes(cfg, ctx, pages) == attn == 67291428
+    assert bench.alg_bytes(cfg, ctx, pages, fused=True) == fused == 67423012
