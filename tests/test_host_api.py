@@ -360,3 +360,17 @@ def test_bench_algorithmic_bytes_of_config_1():
     fused = attn + 2 * B * n_kv * D * e * 2 + 2 * 4 * B
     assert bench.alg_bytes(cfg, ctx, pages) == attn == 67291428
     assert bench.alg_bytes(cfg, ctx, pages, fused=True) == fused == 67423012
+
+
+def test_bench_prefill_flops_count_causal_pairs():
+    """The tensor roofline's numerator for kernel 3: 4 * n_q * D FLOPs (QK^T
+    and PV, a multiply-add each) per causal (row, key) pair, L (L + 1) / 2
+    pairs per prompt of L tokens."""
+    import os
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+
+    B, L, n_q, D = 16, 2048, 32, 128
+    assert bench.prefill_flops(B, L, n_q, D) == B * L * (L + 1) // 2 * 4 * n_q * D == 550024249344
